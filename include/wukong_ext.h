@@ -1,0 +1,81 @@
+/*
+ * wukong_ext.h -- extended C API of the B200 wukong library: a native Llama-3
+ * decode engine with a paged KV cache, batched greedy decode and CUDA-graph
+ * replay.  The reference has no counterpart; its Go runtime drives the same
+ * computation through cuda.h (llm/llama.go:117-154 per step, re-running the
+ * whole sequence).  This API is what bench.py and C hosts use to run the hot
+ * path without re-prefill.
+ *
+ * Conventions: all tensor arguments are device pointers, borrowed (the caller
+ * keeps them alive); weights are raw GGUF bytes in the llama.go layout (fused
+ * q|k|v rows, fused up|gate rows).  Functions return 0 on success and a
+ * negative code on error; wk_last_error() describes the last error.
+ * cuda_init() must have been called first (the engine runs on its stream).
+ */
+#ifndef WUKONG_B200_EXT_H
+#define WUKONG_B200_EXT_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct wk_model wk_model;
+
+typedef struct {
+    int n_layers, d_model, n_heads, n_kv_heads, head_dim, ffn, vocab;
+    float eps;
+    int wtype;       /* dtype of the linear layers (GGML id: 1 F16, 8 Q8_0, 30 BF16) */
+    int out_wtype;   /* dtype of output.weight */
+    int embd_wtype;  /* dtype of token_embd.weight (0 F32, 1 F16, 8 Q8_0, 30 BF16) */
+} wk_config;
+
+const char *wk_last_error(void);
+
+wk_model *wk_model_create(const wk_config *cfg);
+void wk_model_destroy(wk_model *m);
+/* per layer l: attn_norm [d] f32, qkv [(H + 2 Hk) D, d], o [d, d], ffn_norm [d] f32,
+ * fc [2 F, d] (up rows then gate rows), down [d, F] */
+int wk_model_set_layer(wk_model *m, int l, const void *attn_norm, const void *qkv, const void *o,
+                       const void *ffn_norm, const void *fc, const void *down);
+/* token_embd [V, d], output_norm [d] f32, output [V, d], freqs [ctx, D] f32 (cos, sin pairs) */
+int wk_model_set_head(wk_model *m, const void *token_embd, const void *output_norm, const void *output,
+                      const void *freqs, int freqs_ctx);
+/* paged KV cache for up to max_batch sequences of up to max_ctx tokens each */
+int wk_model_alloc_cache(wk_model *m, int max_batch, int max_ctx);
+
+/* Prefill: batch sequences, each with n prompt tokens (device int32 [batch, n]),
+ * positions 0..n-1; writes the greedy next token of each sequence to
+ * tokens_out (device int32 [batch]) and arms the decode state. */
+int wk_model_prefill(wk_model *m, const int *ids, int batch, int n, int *tokens_out);
+/* One greedy decode step for the armed batch: consumes the last tokens,
+ * appends one position, writes the next tokens to the internal token buffer.
+ * The first call captures the step into a CUDA graph; later calls replay it. */
+int wk_model_decode_step(wk_model *m);
+/* device int32 [batch]: tokens produced by the latest prefill / decode step */
+const int *wk_model_tokens(const wk_model *m);
+/* device int32 [batch]: input tokens of the next decode step (writable) */
+int *wk_model_next_ids(wk_model *m);
+/* number of this library's kernel launches in one decode step */
+int wk_model_step_launches(const wk_model *m);
+/* current sequence length (positions used) */
+int wk_model_position(const wk_model *m);
+
+/* Synthetic weights, bit-identical to the CPU oracle's generator:
+ * Irwin-Hall(4) normal(0, stdv) samples of a counter-based hash. */
+int wk_fill_random_q8_0(void *dst, long rows, int cols, uint64_t seed, float stdv);
+int wk_fill_random_f16(void *dst, long n, uint64_t seed, float stdv);
+int wk_fill_const_f32(void *dst, long n, float value);
+
+/* Direct GEMV entry (decode matmul): out[M, N] = x[M, K] . W[N, K]^T, M <= 8,
+ * half activations for F16/Q8_0 weights.  For benchmarking the op alone. */
+int wk_gemv(void *out, const void *x, const void *w, int M, int K, int N, int wtype);
+
+/* library stream (cudaStream_t) so hosts can order their own work */
+void *wk_stream(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -18,3 +18,13 @@ def kat():
     """Known-answer vectors of the reference's own tests (tests/golden/make_golden.py)."""
     with open(os.path.join(ROOT, "tests", "golden", "reference_kat.json")) as f:
         return json.load(f)
+
+
+@pytest.fixture(scope="session")
+def dev():
+    """The library initialised on cuda:0 (cuda_init / cuda_fini)."""
+    import wukong_b200 as wk
+    L = wk.lib()
+    L.cuda_init(0)
+    yield L
+    L.cuda_fini()

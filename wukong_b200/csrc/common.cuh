@@ -1,0 +1,218 @@
+// Shared definitions of the B200 (sm_100a) wukong op library.
+//
+// The library sits behind the reference's flat C ABI (cuda.h of liuy/wukong) and
+// an extended wk_* API.  It deliberately avoids the C++ runtime library (no
+// new/delete, no STL containers, no exceptions) so that the static archive links
+// with exactly the cgo line of llm/array.go:4
+// (-lcublasLt -lcudart -lm -lcublas).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+namespace wk {
+
+// GGML dtype ids (the reference's wukong.h:15-52 enum, llm/array.go:23-61).
+enum DType : int {
+    kF32 = 0,
+    kF16 = 1,
+    kQ8_0 = 8,
+    kBF16 = 30,
+    kDTypeCount = 36,
+};
+
+struct DTypeInfo {
+    const char *name;
+    int block_size;
+    int type_size;
+};
+extern const DTypeInfo kDTypes[kDTypeCount];
+
+// Q8_0 block: fp16 scale followed by 32 int8 quants, 34 bytes, no padding.
+constexpr int kQ8Block = 32;
+constexpr int kQ8Bytes = 34;
+
+// Activation element type that the reference instantiates for a weight dtype:
+// float for F32, bf16 for BF16, half for F16 and every quantised type
+// (cuda.cu:1324-1338).
+inline int act_of(int wtype) { return wtype == kF32 ? kF32 : (wtype == kBF16 ? kBF16 : kF16); }
+inline size_t act_size(int act) { return act == kF32 ? 4 : 2; }
+
+// ---------------------------------------------------------------- errors
+[[noreturn]] void panic_impl(const char *file, int line, const char *func, const char *fmt, ...);
+#define WK_PANIC(...) ::wk::panic_impl(__FILE__, __LINE__, __func__, __VA_ARGS__)
+#define WK_CHECK(call)                                                                          \
+    do {                                                                                        \
+        cudaError_t e_ = (call);                                                                \
+        if (e_ != cudaSuccess) WK_PANIC("CUDA error (%d): %s", (int)e_, cudaGetErrorString(e_)); \
+    } while (0)
+#define WK_CHECK_LAUNCH() WK_CHECK(cudaGetLastError())
+
+// ---------------------------------------------------------------- runtime state
+struct Runtime {
+    int device = -1;
+    int num_sms = 0;
+    int max_smem_optin = 0;
+    cudaStream_t stream = nullptr;
+    // device-side error word (mapped pinned memory): bounded waits that give up
+    // set a code here
+    int *d_error = nullptr;
+    int *h_error = nullptr;
+    // grow-only scratch arena for op temporaries (stream ordered on `stream`)
+    void *ws = nullptr;
+    size_t ws_size = 0;
+    bool pdl = true;  // programmatic dependent launch on the hot kernels
+};
+extern Runtime g_rt;
+
+void ensure_init();
+// Scratch memory valid until the next call that asks for scratch.
+void *scratch(size_t bytes);
+inline cudaStream_t stream() { return g_rt.stream; }
+void set_device_current();
+void check_device_error();
+
+// ---------------------------------------------------------------- device helpers
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <typename T> struct Act;
+template <> struct Act<float> {
+    static __device__ __forceinline__ float load(const float *p) { return *p; }
+    static __device__ __forceinline__ float to_f(float v) { return v; }
+    static __device__ __forceinline__ float from_f(float v) { return v; }
+    static __device__ __forceinline__ float round(float v) { return v; }
+};
+template <> struct Act<__half> {
+    static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+    static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+    static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
+};
+template <> struct Act<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+    static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+};
+
+__device__ __forceinline__ float to_float(float v) { return v; }
+__device__ __forceinline__ float to_float(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> __device__ __forceinline__ T from_float(float v);
+template <> __device__ __forceinline__ float from_float<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
+    return __float2bfloat16_rn(v);
+}
+template <typename T> __device__ __forceinline__ float round_to(float v) { return to_float(from_float<T>(v)); }
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: gives up after one second (far above any legitimate wait for a
+// bulk copy), records `code` in the device error word and returns false.  The
+// caller keeps its control flow uniform so that no other warp is left waiting.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > 1000000000ull) break;
+    }
+    if (err) atomicCAS(err, 0, code);
+    return false;
+}
+// 1-D bulk copy global -> shared, completing on `bar` (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Four int8 quants (one 32-bit word, bytes q0..q3) -> two half2 {q0,q1},{q2,q3},
+// exact: byte b is placed as the mantissa of 1024 + (b ^ 0x80), then 1152 is
+// subtracted (all values are integers below 2048, so no rounding occurs).
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, __half2 &lo, __half2 &hi) {
+    const uint32_t x = w ^ 0x80808080u;
+    uint32_t l = __byte_perm(x, 0x64646464u, 0x5140);  // {0x64, b1, 0x64, b0}
+    uint32_t h = __byte_perm(x, 0x64646464u, 0x5342);  // {0x64, b3, 0x64, b2}
+    const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152.0
+    lo = __hsub2(*reinterpret_cast<__half2 *>(&l), bias);
+    hi = __hsub2(*reinterpret_cast<__half2 *>(&h), bias);
+}
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
+
+}  // namespace wk

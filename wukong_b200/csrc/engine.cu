@@ -1,0 +1,544 @@
+// Native Llama-3 decode engine (wukong_ext.h): paged KV cache, batched greedy
+// decode, CUDA-graph replay of the decode step with on-device token feedback.
+//
+// One decode step for B sequences is 5 launches per layer plus 3:
+//   embed (gather + convert) -> per layer { QKV GEMV [RMSNorm | RoPE + KV append],
+//   attention, O GEMV [+residual], FC GEMV [RMSNorm | SwiGLU], down GEMV
+//   [+residual] } -> logits GEMV [RMSNorm | argmax] -> advance (ids <- tokens,
+//   pos += 1).
+// The GEMVs and attention are launched with programmatic dependent launch, so
+// inside the graph each kernel starts streaming its weights while the previous
+// one drains.  The reference computes the same step by re-running the whole
+// sequence through cuda.h (llm/llama.go:117-154, llm/model.go:158).
+#include <stdarg.h>
+
+#include "common.cuh"
+#include "wukong_ext.h"
+#include "wukong_internal.cuh"
+
+namespace wk {
+
+namespace {
+
+char g_err[512] = "";
+
+int fail(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return -1;
+}
+
+#define WK_TRY(call)                                                                 \
+    do {                                                                             \
+        cudaError_t e_ = (call);                                                     \
+        if (e_ != cudaSuccess) return fail("%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+constexpr int kPage = 64;
+
+struct Layer {
+    const float *attn_norm = nullptr, *ffn_norm = nullptr;
+    const uint8_t *qkv = nullptr, *o = nullptr, *fc = nullptr, *down = nullptr;
+};
+
+// ------------------------------------------------------------ small kernels
+__global__ void advance_kernel(int *ids, const int *tokens, int *pos, int batch) {
+    int b = threadIdx.x + blockIdx.x * blockDim.x;
+    if (b < batch) {
+        ids[b] = tokens[b];
+        pos[b] += 1;
+    }
+}
+
+__global__ void iota_kernel(int *p, int n, int v0, int step) {
+    int i = threadIdx.x + blockIdx.x * blockDim.x;
+    if (i < n) p[i] = v0 + i * step;
+}
+
+__global__ void fill_i32_kernel(int *p, int n, int v) {
+    int i = threadIdx.x + blockIdx.x * blockDim.x;
+    if (i < n) p[i] = v;
+}
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+// Irwin-Hall(4) of 16-bit uniforms, integer exact (matches the CPU oracle bit for bit)
+__device__ __forceinline__ float gen_one(uint64_t seed, uint64_t idx, float k) {
+    uint64_t h = mix64(seed + (idx + 1) * 0x9E3779B97F4A7C15ull);
+    int32_t s = (int32_t)(h & 0xffff) + (int32_t)((h >> 16) & 0xffff) + (int32_t)((h >> 32) & 0xffff) +
+                (int32_t)((h >> 48) & 0xffff);
+    return (float)(s - 131070) * k;
+}
+
+__global__ void fill_q8_0_kernel(uint8_t *dst, long nblk, uint64_t seed, float k) {
+    long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblk) return;
+    float x[32];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        x[i] = gen_one(seed, (uint64_t)(b * 32 + i), k);
+        amax = fmaxf(amax, fabsf(x[i]));
+    }
+    const float d = amax / 127.0f;
+    const __half hs = __float2half_rn(d);
+    uint8_t *o = dst + b * 34;
+    const unsigned short bits = __half_as_ushort(hs);
+    o[0] = (uint8_t)(bits & 0xff);
+    o[1] = (uint8_t)(bits >> 8);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        float q = d != 0.f ? roundf(x[i] / d) : 0.f;
+        q = fminf(127.f, fmaxf(-127.f, q));
+        o[2 + i] = (uint8_t)(int8_t)q;
+    }
+}
+
+__global__ void fill_f16_kernel(__half *dst, long n, uint64_t seed, float k) {
+    long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = __float2half_rn(gen_one(seed, (uint64_t)i, k));
+}
+
+__global__ void fill_f32_kernel(float *dst, long n, float v) {
+    long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = v;
+}
+
+// token gather converted to the activation type (F32 / F16 / BF16 / Q8_0 tables)
+template <typename T>
+__global__ void embed_kernel(T *__restrict__ out, const int *__restrict__ ids, const uint8_t *__restrict__ table,
+                             int col, int dtype, int vocab, int *err) {
+    const int r = blockIdx.x;
+    long id = ids[r];
+    if (id < 0 || id >= vocab) {
+        // an out-of-range id (e.g. -1 from an all-NaN argmax) is reported, never dereferenced
+        if (threadIdx.x == 0 && err) atomicCAS(err, 0, 2);
+        id = 0;
+    }
+    for (int i = threadIdx.x; i < col; i += blockDim.x) {
+        float v;
+        if (dtype == kQ8_0) {
+            const uint8_t *blk = table + (id * (col / 32) + i / 32) * 34;
+            const float s = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+            v = __half2float(__float2half_rn(s * (float)(int8_t)blk[2 + (i & 31)]));
+        } else if (dtype == kF16) {
+            v = __half2float(reinterpret_cast<const __half *>(table)[id * col + i]);
+        } else if (dtype == kBF16) {
+            v = __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(table)[id * col + i]);
+        } else {
+            v = reinterpret_cast<const float *>(table)[id * col + i];
+        }
+        out[(long)r * col + i] = from_float<T>(v);
+    }
+}
+
+}  // namespace
+}  // namespace wk
+
+using namespace wk;
+
+struct wk_model {
+    wk_config cfg;
+    int act = kF16;
+    Layer *layers = nullptr;
+    const uint8_t *embd = nullptr, *out_w = nullptr;
+    const float *out_norm = nullptr, *freqs = nullptr;
+    int freqs_ctx = 0;
+    // paged cache: pool[l] = [max_batch * max_pages][Hk][kPage][D]
+    int max_batch = 0, max_ctx = 0, max_pages = 0;
+    void **kpool = nullptr, **vpool = nullptr;
+    int *block_table = nullptr;
+    // decode state
+    int batch = 0, pos = 0;
+    int *d_pos = nullptr, *d_seq = nullptr, *d_ids = nullptr, *d_tokens = nullptr;
+    int *d_row_seq = nullptr, *d_row_pos = nullptr;
+    // activations
+    int rows_cap = 0;
+    void *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
+    // logits argmax partials
+    float *part_val = nullptr;
+    unsigned long long *part_key = nullptr;
+    int *counter = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    int graph_batch = 0;
+    int step_launches = 0;
+};
+
+namespace {
+
+int ensure_rows(wk_model *m, int rows) {
+    if (rows <= m->rows_cap) return 0;
+    const wk_config &c = m->cfg;
+    const size_t es = act_size(m->act);
+    cudaStream_t s = stream();
+    for (void **p : {&m->x, &m->q, &m->att, &m->h})
+        if (*p) WK_TRY(cudaFreeAsync(*p, s));
+    for (int **p : {&m->d_row_seq, &m->d_row_pos})
+        if (*p) WK_TRY(cudaFreeAsync(*p, s));
+    WK_TRY(cudaMallocAsync(&m->x, es * rows * c.d_model, s));
+    WK_TRY(cudaMallocAsync(&m->q, es * rows * c.n_heads * c.head_dim, s));
+    WK_TRY(cudaMallocAsync(&m->att, es * rows * c.n_heads * c.head_dim, s));
+    WK_TRY(cudaMallocAsync(&m->h, es * rows * c.ffn, s));
+    WK_TRY(cudaMallocAsync(&m->d_row_seq, sizeof(int) * rows, s));
+    WK_TRY(cudaMallocAsync(&m->d_row_pos, sizeof(int) * rows, s));
+    m->rows_cap = rows;
+    return 0;
+}
+
+// Run the layers and the logits head on `rows` activation rows in m->x.
+// Row i belongs to sequence seq[i] at position pos[i]; max_len bounds the
+// attention length.  Returns the number of kernel launches.
+int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_len, int batch, int last_row_stride,
+               int *tokens) {
+    const wk_config &c = m->cfg;
+    const size_t es = act_size(m->act);
+    const int d = c.d_model, col = c.n_heads * c.head_dim;
+    cudaStream_t s = stream();
+    PagedKV kv;
+    kv.block_table = m->block_table;
+    kv.max_pages = m->max_pages;
+    kv.page = kPage;
+    kv.kv_heads = c.n_kv_heads;
+    kv.hd = c.head_dim;
+    int launches = 0;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const Layer &L = m->layers[l];
+        kv.k = m->kpool[l];
+        kv.v = m->vpool[l];
+        for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
+            GemvArgs a;
+            a.w = L.qkv;
+            a.wtype = c.wtype;
+            a.N = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+            a.K = d;
+            a.x = (const char *)m->x + (size_t)m0 * d * es;
+            a.ldx = d;
+            a.M = rows - m0 < 8 ? rows - m0 : 8;
+            a.norm_w = L.attn_norm;
+            a.eps = c.eps;
+            a.epi = EPI_QKV;
+            a.out = (char *)m->q + (size_t)m0 * col * es;
+            a.ldo = col;
+            a.nq = c.n_heads * c.head_dim;
+            a.nk = c.n_kv_heads * c.head_dim;
+            a.hd = c.head_dim;
+            a.freqs = m->freqs;
+            a.pos = pos + m0;
+            a.seq = seq + m0;
+            a.kpool = kv.k;
+            a.vpool = kv.v;
+            a.block_table = kv.block_table;
+            a.max_pages = kv.max_pages;
+            a.page = kPage;
+            a.kv_heads = c.n_kv_heads;
+            gemv(a, m->act, s);
+        }
+        if (m->act == kF16)
+            attention_paged<__half>((__half *)m->att, col, (const __half *)m->q, col, seq, pos, rows, max_len, kv,
+                                    c.n_heads, s, true);
+        else
+            attention_paged<__nv_bfloat16>((__nv_bfloat16 *)m->att, col, (const __nv_bfloat16 *)m->q, col, seq, pos,
+                                           rows, max_len, kv, c.n_heads, s, true);
+        ++launches;
+        for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
+            GemvArgs a;
+            a.w = L.o;
+            a.wtype = c.wtype;
+            a.N = d;
+            a.K = col;
+            a.x = (const char *)m->att + (size_t)m0 * col * es;
+            a.ldx = col;
+            a.M = rows - m0 < 8 ? rows - m0 : 8;
+            a.epi = EPI_RESID;
+            a.out = (char *)m->x + (size_t)m0 * d * es;
+            a.ldo = d;
+            a.res = a.out;
+            a.ldr = d;
+            gemv(a, m->act, s);
+        }
+        for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
+            GemvArgs a;
+            a.w = L.fc;
+            a.wtype = c.wtype;
+            a.N = 2 * c.ffn;
+            a.K = d;
+            a.x = (const char *)m->x + (size_t)m0 * d * es;
+            a.ldx = d;
+            a.M = rows - m0 < 8 ? rows - m0 : 8;
+            a.norm_w = L.ffn_norm;
+            a.eps = c.eps;
+            a.epi = EPI_SWIGLU;
+            a.F = c.ffn;
+            a.out = (char *)m->h + (size_t)m0 * c.ffn * es;
+            a.ldo = c.ffn;
+            gemv(a, m->act, s);
+        }
+        for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
+            GemvArgs a;
+            a.w = L.down;
+            a.wtype = c.wtype;
+            a.N = d;
+            a.K = c.ffn;
+            a.x = (const char *)m->h + (size_t)m0 * c.ffn * es;
+            a.ldx = c.ffn;
+            a.M = rows - m0 < 8 ? rows - m0 : 8;
+            a.epi = EPI_RESID;
+            a.out = (char *)m->x + (size_t)m0 * d * es;
+            a.ldo = d;
+            a.res = a.out;
+            a.ldr = d;
+            gemv(a, m->act, s);
+        }
+    }
+    // logits + argmax on the last row of each sequence
+    for (int b0 = 0; b0 < batch; b0 += 8, ++launches) {
+        GemvArgs a;
+        a.w = m->out_w;
+        a.wtype = c.out_wtype;
+        a.N = c.vocab;
+        a.K = d;
+        a.x = (const char *)m->x + ((size_t)b0 * last_row_stride + (last_row_stride - 1)) * d * es;
+        a.ldx = (long)last_row_stride * d;
+        a.M = batch - b0 < 8 ? batch - b0 : 8;
+        a.norm_w = m->out_norm;
+        a.eps = c.eps;
+        a.epi = EPI_LOGITS;
+        a.part_val = m->part_val;
+        a.part_key = m->part_key;
+        a.counter = m->counter;
+        a.tokens = tokens + b0;
+        a.pack = 16 / (int)es;
+        gemv(a, m->act, s);
+    }
+    return launches;
+}
+
+void launch_embed(wk_model *m, const int *ids, int rows) {
+    const wk_config &c = m->cfg;
+    if (m->act == kF16)
+        embed_kernel<__half><<<rows, 256, 0, stream()>>>((__half *)m->x, ids, m->embd, c.d_model, c.embd_wtype,
+                                                         c.vocab, g_rt.d_error);
+    else
+        embed_kernel<__nv_bfloat16><<<rows, 256, 0, stream()>>>((__nv_bfloat16 *)m->x, ids, m->embd, c.d_model,
+                                                                c.embd_wtype, c.vocab, g_rt.d_error);
+    WK_CHECK_LAUNCH();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *wk_last_error(void) { return g_err; }
+
+void *wk_stream(void) { return (void *)stream(); }
+
+wk_model *wk_model_create(const wk_config *cfg) {
+    if (g_rt.device < 0) {
+        fail("cuda_init() has not been called");
+        return nullptr;
+    }
+    set_device_current();
+    const wk_config &c = *cfg;
+    if (c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads || c.n_heads * c.head_dim != c.d_model || c.head_dim % 2) {
+        fail("inconsistent attention geometry");
+        return nullptr;
+    }
+    const int act = act_of(c.wtype);
+    if (act == kF32 || !gemv_supported(c.wtype, act, c.d_model) || !gemv_supported(c.wtype, act, c.ffn) ||
+        !gemv_supported(c.out_wtype, act, c.d_model)) {
+        fail("the engine needs F16 / BF16 / Q8_0 weights with 16/32-aligned widths");
+        return nullptr;
+    }
+    wk_model *m = (wk_model *)calloc(1, sizeof(wk_model));
+    m->cfg = c;
+    m->act = act;
+    m->layers = (Layer *)calloc(c.n_layers, sizeof(Layer));
+    cudaStream_t s = stream();
+    if (cudaMallocAsync(&m->part_val, sizeof(float) * kMaxLogitCtas * 8, s) != cudaSuccess ||
+        cudaMallocAsync(&m->part_key, sizeof(unsigned long long) * kMaxLogitCtas * 8, s) != cudaSuccess ||
+        cudaMallocAsync(&m->counter, sizeof(int), s) != cudaSuccess ||
+        cudaMemsetAsync(m->counter, 0, sizeof(int), s) != cudaSuccess) {
+        fail("allocation failed");
+        free(m->layers);
+        free(m);
+        return nullptr;
+    }
+    return m;
+}
+
+void wk_model_destroy(wk_model *m) {
+    if (!m) return;
+    set_device_current();
+    cudaStream_t s = stream();
+    cudaStreamSynchronize(s);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    for (int l = 0; m->kpool && l < m->cfg.n_layers; ++l) {
+        cudaFree(m->kpool[l]);
+        cudaFree(m->vpool[l]);
+    }
+    free(m->kpool);
+    free(m->vpool);
+    void *bufs[] = {m->block_table, m->d_pos, m->d_seq, m->d_ids, m->d_tokens, m->d_row_seq, m->d_row_pos,
+                    m->x, m->q, m->att, m->h, m->part_val, m->part_key, m->counter};
+    for (void *p : bufs)
+        if (p) cudaFree(p);
+    free(m->layers);
+    free(m);
+}
+
+int wk_model_set_layer(wk_model *m, int l, const void *attn_norm, const void *qkv, const void *o,
+                       const void *ffn_norm, const void *fc, const void *down) {
+    if (!m || l < 0 || l >= m->cfg.n_layers) return fail("bad layer index %d", l);
+    Layer &L = m->layers[l];
+    L.attn_norm = (const float *)attn_norm;
+    L.qkv = (const uint8_t *)qkv;
+    L.o = (const uint8_t *)o;
+    L.ffn_norm = (const float *)ffn_norm;
+    L.fc = (const uint8_t *)fc;
+    L.down = (const uint8_t *)down;
+    return 0;
+}
+
+int wk_model_set_head(wk_model *m, const void *token_embd, const void *output_norm, const void *output,
+                      const void *freqs, int freqs_ctx) {
+    if (!m) return fail("null model");
+    m->embd = (const uint8_t *)token_embd;
+    m->out_norm = (const float *)output_norm;
+    m->out_w = (const uint8_t *)output;
+    m->freqs = (const float *)freqs;
+    m->freqs_ctx = freqs_ctx;
+    return 0;
+}
+
+int wk_model_alloc_cache(wk_model *m, int max_batch, int max_ctx) {
+    if (!m || max_batch <= 0 || max_ctx <= 0) return fail("bad cache size");
+    set_device_current();
+    const wk_config &c = m->cfg;
+    cudaStream_t s = stream();
+    m->max_batch = max_batch;
+    m->max_ctx = max_ctx;
+    m->max_pages = (max_ctx + kPage - 1) / kPage;
+    const size_t page_bytes = (size_t)c.n_kv_heads * kPage * c.head_dim * act_size(m->act);
+    m->kpool = (void **)calloc(c.n_layers, sizeof(void *));
+    m->vpool = (void **)calloc(c.n_layers, sizeof(void *));
+    for (int l = 0; l < c.n_layers; ++l) {
+        WK_TRY(cudaMalloc(&m->kpool[l], page_bytes * max_batch * m->max_pages));
+        WK_TRY(cudaMalloc(&m->vpool[l], page_bytes * max_batch * m->max_pages));
+    }
+    WK_TRY(cudaMallocAsync(&m->block_table, sizeof(int) * max_batch * m->max_pages, s));
+    fill_block_table(m->block_table, max_batch, m->max_pages, s);
+    for (int **p : {&m->d_pos, &m->d_seq, &m->d_ids, &m->d_tokens}) WK_TRY(cudaMallocAsync(p, sizeof(int) * max_batch, s));
+    iota_kernel<<<(max_batch + 127) / 128, 128, 0, s>>>(m->d_seq, max_batch, 0, 1);
+    WK_TRY(cudaGetLastError());
+    return 0;
+}
+
+int wk_model_prefill(wk_model *m, const int *ids, int batch, int n, int *tokens_out) {
+    if (!m || !m->kpool) return fail("cache not allocated");
+    if (batch <= 0 || batch > m->max_batch || n <= 0 || n > m->max_ctx || n > m->freqs_ctx)
+        return fail("prefill batch %d x %d exceeds the cache (%d x %d)", batch, n, m->max_batch, m->max_ctx);
+    set_device_current();
+    const int rows = batch * n;
+    if (ensure_rows(m, rows < 8 * batch ? 8 * batch : rows)) return -1;
+    cudaStream_t s = stream();
+    fill_row_meta(m->d_row_seq, m->d_row_pos, rows, n, 0, s);
+    launch_embed(m, ids, rows);
+    run_layers(m, rows, m->d_row_seq, m->d_row_pos, n, batch, n, m->d_tokens);
+    // arm decode: next inputs are the predicted tokens at position n
+    WK_TRY(cudaMemcpyAsync(m->d_ids, m->d_tokens, sizeof(int) * batch, cudaMemcpyDeviceToDevice, s));
+    fill_i32_kernel<<<(batch + 127) / 128, 128, 0, s>>>(m->d_pos, batch, n);
+    WK_TRY(cudaGetLastError());
+    if (tokens_out) WK_TRY(cudaMemcpyAsync(tokens_out, m->d_tokens, sizeof(int) * batch, cudaMemcpyDeviceToDevice, s));
+    if (m->graph && m->graph_batch != batch) {
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    m->batch = batch;
+    m->pos = n;
+    return 0;
+}
+
+int wk_model_decode_step(wk_model *m) {
+    if (!m || m->batch <= 0) return fail("no armed batch (call wk_model_prefill first)");
+    if (m->pos + 1 > m->max_ctx || m->pos + 1 > m->freqs_ctx) return fail("context full (%d)", m->pos);
+    set_device_current();
+    cudaStream_t s = stream();
+    const int B = m->batch;
+    if (!m->graph) {
+        if (ensure_rows(m, 8 * B)) return -1;
+        WK_TRY(cudaStreamSynchronize(s));
+        cudaGraph_t g;
+        WK_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        launch_embed(m, m->d_ids, B);
+        int n = 1 + run_layers(m, B, m->d_seq, m->d_pos, m->max_ctx, B, 1, m->d_tokens);
+        advance_kernel<<<(B + 127) / 128, 128, 0, s>>>(m->d_ids, m->d_tokens, m->d_pos, B);
+        n += 1;
+        cudaError_t e = cudaGetLastError();
+        cudaError_t e2 = cudaStreamEndCapture(s, &g);
+        if (e != cudaSuccess || e2 != cudaSuccess)
+            return fail("graph capture failed: %s / %s", cudaGetErrorString(e), cudaGetErrorString(e2));
+        WK_TRY(cudaGraphInstantiate(&m->graph, g, 0));
+        cudaGraphDestroy(g);
+        m->graph_batch = B;
+        m->step_launches = n;
+    }
+    WK_TRY(cudaGraphLaunch(m->graph, s));
+    m->pos += 1;
+    return 0;
+}
+
+const int *wk_model_tokens(const wk_model *m) { return m ? m->d_tokens : nullptr; }
+int *wk_model_next_ids(wk_model *m) { return m ? m->d_ids : nullptr; }
+int wk_model_step_launches(const wk_model *m) { return m ? m->step_launches : 0; }
+int wk_model_position(const wk_model *m) { return m ? m->pos : 0; }
+
+int wk_fill_random_q8_0(void *dst, long rows, int cols, uint64_t seed, float stdv) {
+    if (cols % 32) return fail("cols must be a multiple of 32");
+    ensure_init();
+    const long nblk = rows * (cols / 32);
+    const float k = stdv / 37837.227f;
+    fill_q8_0_kernel<<<(unsigned)((nblk + 255) / 256), 256, 0, stream()>>>((uint8_t *)dst, nblk, seed, k);
+    WK_TRY(cudaGetLastError());
+    return 0;
+}
+
+int wk_fill_random_f16(void *dst, long n, uint64_t seed, float stdv) {
+    ensure_init();
+    const float k = stdv / 37837.227f;
+    fill_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream()>>>((__half *)dst, n, seed, k);
+    WK_TRY(cudaGetLastError());
+    return 0;
+}
+
+int wk_fill_const_f32(void *dst, long n, float value) {
+    ensure_init();
+    fill_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream()>>>((float *)dst, n, value);
+    WK_TRY(cudaGetLastError());
+    return 0;
+}
+
+int wk_gemv(void *out, const void *x, const void *w, int M, int K, int N, int wtype) {
+    ensure_init();
+    const int act = act_of(wtype);
+    if (M < 1 || M > 8 || !gemv_supported(wtype, act, K)) return fail("wk_gemv: unsupported shape/dtype");
+    GemvArgs a;
+    a.w = (const uint8_t *)w;
+    a.wtype = wtype;
+    a.N = N;
+    a.K = K;
+    a.x = x;
+    a.ldx = K;
+    a.M = M;
+    a.epi = EPI_STORE;
+    a.out = out;
+    a.ldo = N;
+    gemv(a, act, stream());
+    return 0;
+}
+
+}  // extern "C"

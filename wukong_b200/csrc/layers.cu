@@ -1,0 +1,666 @@
+// Layer drivers of the C ABI (cuda.h:21, :23, :25, :27) and the prefix cache.
+//
+// Reference call sequence (cuda.cu:902-990):
+//   group_query_attention: rmsnorm -> matmul(qkv) -> rope -> repeat -> sdpa
+//                          -> matmul(o) -> add(residual)
+//   feed_forward:          rmsnorm -> matmul(up|gate) -> swiglu -> matmul(down)
+//                          -> add(residual)
+//   classify / predict:    last row -> rmsnorm -> matmul(vocab) [-> argmax]
+// Here, for 16-bit and Q8_0 weights, each sublayer is two or three launches:
+//   QKV GEMV  (RMSNorm prologue; RoPE + K/V append to a paged cache epilogue)
+//   attention (GQA group per CTA, reference rounding points)
+//   O GEMV    (residual-add epilogue)
+//   FC GEMV   (RMSNorm prologue; SwiGLU epilogue pairing up and gate rows)
+//   down GEMV (residual-add epilogue)
+//   logits    (RMSNorm prologue; argmax epilogue)
+// F32 weights take the unfused reference-shaped path with the generic kernels.
+//
+// Prefix cache (opt-in, WUKONG_PREFIX_CACHE=1).  The reference's Go loop
+// re-sends the whole token sequence every step (llm/model.go:158,175) and the
+// ABI has no KV-cache notion.  With the cache on, the library keeps each
+// layer's K/V (keyed by the qkv weight pointer) for the ids of the last
+// completed forward pass (embedding -> layers -> predict/classify), recognises
+// a repeated prefix in the next cuda_embedding call (the ids are read from the
+// host copy handed to cuda_to_device), and computes only the new rows.  Rows of
+// `embeds` below the reused prefix are then left unwritten: the ABI result is
+// exact for the rows that cuda_predict/cuda_classify read (the last row of each
+// batch), which is all the reference's Go code reads.  Off by default.
+#include "common.cuh"
+#include "wukong_internal.cuh"
+
+namespace wk {
+
+namespace {
+
+constexpr int kPage = 64;       // tokens per KV page
+constexpr int kMaxLayers = 256;
+constexpr int kMaxShadows = 8;
+
+struct LayerKV {
+    const void *qkv_w = nullptr;
+    void *k = nullptr, *v = nullptr;  // [batch * max_pages][kv_heads][kPage][hd]
+    int valid = 0;                    // rows whose K/V are cached
+};
+
+struct Session {
+    bool enabled = false;
+    const void *embd = nullptr;  // token table (model identity)
+    int batch = 0, kv_heads = 0, hd = 0, act = kF16;
+    int max_pages = 0;
+    int *block_table = nullptr;  // device [batch][max_pages], identity
+    int *ids = nullptr;          // host [batch][ids_cap] ids of the last completed pass
+    int ids_cap = 0, completed = 0;
+    // pass in flight
+    bool active = false;
+    void *embeds = nullptr;
+    int row = 0, P = 0;
+    int *new_ids = nullptr;  // host copy of this pass's ids
+    LayerKV layers[kMaxLayers];
+    int nlayers = 0;
+};
+
+struct Shadow {
+    void *dst = nullptr;
+    size_t size = 0;
+    int *host = nullptr;
+};
+
+Session g_sess;
+Shadow g_shadow[kMaxShadows];
+int g_shadow_next = 0;
+
+// ---------------------------------------------------------------- scratch carving
+struct Carver {
+    char *base;
+    size_t off = 0;
+    explicit Carver(void *b) : base((char *)b) {}
+    template <typename U> U *take(size_t n) {
+        off = (off + 255) & ~(size_t)255;
+        U *p = (U *)(base + off);
+        off += n * sizeof(U);
+        return p;
+    }
+    static size_t round(size_t n) { return (n + 255) & ~(size_t)255; }
+};
+
+void drop_session_layers() {
+    for (int i = 0; i < g_sess.nlayers; ++i) {
+        if (g_sess.layers[i].k) WK_CHECK(cudaFreeAsync(g_sess.layers[i].k, stream()));
+        if (g_sess.layers[i].v) WK_CHECK(cudaFreeAsync(g_sess.layers[i].v, stream()));
+        g_sess.layers[i] = LayerKV();
+    }
+    g_sess.nlayers = 0;
+    if (g_sess.block_table) WK_CHECK(cudaFreeAsync(g_sess.block_table, stream()));
+    g_sess.block_table = nullptr;
+    g_sess.max_pages = 0;
+    g_sess.completed = 0;
+}
+
+// grow every layer pool (and the shared identity block table) to `pages` per sequence
+void session_reserve(int rows) {
+    const int need = (rows + kPage - 1) / kPage;
+    if (need <= g_sess.max_pages) return;
+    int np = g_sess.max_pages ? g_sess.max_pages : 4;
+    while (np < need) np *= 2;
+    const size_t es = act_size(g_sess.act);
+    const size_t page_bytes = (size_t)g_sess.kv_heads * kPage * g_sess.hd * es;
+    for (int i = 0; i < g_sess.nlayers; ++i) {
+        LayerKV &L = g_sess.layers[i];
+        void *nk, *nv;
+        WK_CHECK(cudaMallocAsync(&nk, page_bytes * g_sess.batch * np, stream()));
+        WK_CHECK(cudaMallocAsync(&nv, page_bytes * g_sess.batch * np, stream()));
+        if (L.k && g_sess.max_pages) {
+            // page (b, p) moves from b * old + p to b * np + p
+            WK_CHECK(cudaMemcpy2DAsync(nk, page_bytes * np, L.k, page_bytes * g_sess.max_pages,
+                                       page_bytes * g_sess.max_pages, g_sess.batch, cudaMemcpyDeviceToDevice,
+                                       stream()));
+            WK_CHECK(cudaMemcpy2DAsync(nv, page_bytes * np, L.v, page_bytes * g_sess.max_pages,
+                                       page_bytes * g_sess.max_pages, g_sess.batch, cudaMemcpyDeviceToDevice,
+                                       stream()));
+        }
+        if (L.k) WK_CHECK(cudaFreeAsync(L.k, stream()));
+        if (L.v) WK_CHECK(cudaFreeAsync(L.v, stream()));
+        L.k = nk;
+        L.v = nv;
+    }
+    if (g_sess.block_table) WK_CHECK(cudaFreeAsync(g_sess.block_table, stream()));
+    WK_CHECK(cudaMallocAsync(&g_sess.block_table, sizeof(int) * g_sess.batch * np, stream()));
+    fill_block_table(g_sess.block_table, g_sess.batch, np, stream());
+    g_sess.max_pages = np;
+}
+
+LayerKV *session_layer(const void *qkv_w) {
+    for (int i = 0; i < g_sess.nlayers; ++i)
+        if (g_sess.layers[i].qkv_w == qkv_w) return &g_sess.layers[i];
+    if (g_sess.P > 0)
+        WK_PANIC("prefix cache: a layer that was not part of the previous pass appeared; "
+                 "run with WUKONG_PREFIX_CACHE=0 when the layer set changes between calls");
+    if (g_sess.nlayers == kMaxLayers) WK_PANIC("prefix cache: more than %d layers", kMaxLayers);
+    LayerKV &L = g_sess.layers[g_sess.nlayers++];
+    L.qkv_w = qkv_w;
+    const size_t page_bytes = (size_t)g_sess.kv_heads * kPage * g_sess.hd * act_size(g_sess.act);
+    if (g_sess.max_pages) {
+        WK_CHECK(cudaMallocAsync(&L.k, page_bytes * g_sess.batch * g_sess.max_pages, stream()));
+        WK_CHECK(cudaMallocAsync(&L.v, page_bytes * g_sess.batch * g_sess.max_pages, stream()));
+    }
+    return &L;
+}
+
+const int *find_shadow(const void *ptr, size_t need) {
+    for (int i = 0; i < kMaxShadows; ++i)
+        if (g_shadow[i].dst == ptr && g_shadow[i].size >= need) return g_shadow[i].host;
+    return nullptr;
+}
+
+// Rows [P, row) of every batch are the rows this call computes.
+struct Rows {
+    int P = 0, n = 0;
+    bool cached = false;
+};
+
+Rows plan_rows(const void *x, int batch, int row) {
+    Rows r;
+    r.n = row;
+    if (g_sess.enabled && g_sess.active && x == g_sess.embeds && batch == g_sess.batch && row == g_sess.row) {
+        r.P = g_sess.P;
+        r.n = row - g_sess.P;
+        r.cached = true;
+    }
+    return r;
+}
+
+// gather rows [P, row) of each batch into a contiguous [batch * n, col] block
+void *gather_new_rows(void *x, int batch, int row, int col, int P, size_t es, void *dst) {
+    if (P == 0 || batch == 1) return (char *)x + (size_t)P * col * es;
+    const int n = row - P;
+    WK_CHECK(cudaMemcpy2DAsync(dst, (size_t)n * col * es, (char *)x + (size_t)P * col * es, (size_t)row * col * es,
+                               (size_t)n * col * es, batch, cudaMemcpyDeviceToDevice, stream()));
+    return dst;
+}
+void scatter_new_rows(void *x, const void *src, int batch, int row, int col, int P, size_t es) {
+    if (P == 0 || batch == 1) return;
+    const int n = row - P;
+    WK_CHECK(cudaMemcpy2DAsync((char *)x + (size_t)P * col * es, (size_t)row * col * es, src, (size_t)n * col * es,
+                               (size_t)n * col * es, batch, cudaMemcpyDeviceToDevice, stream()));
+}
+
+// ---------------------------------------------------------------- GQA sublayer
+void gqa_fused(void *out, const void *embeds, const float *freqs, const float *norm_w, const void *qkv_w,
+               const void *out_w, int batch, int row, int NH, int kvNH, int HS, float eps, int wtype) {
+    const int act = act_of(wtype);
+    const size_t es = act_size(act);
+    const int col = NH * HS, W = (NH + 2 * kvNH) * HS;
+    if (out != embeds)
+        WK_CHECK(cudaMemcpyAsync(out, embeds, (size_t)batch * row * col * es, cudaMemcpyDeviceToDevice, stream()));
+    Rows r = plan_rows(out, batch, row);
+    const int rows = batch * r.n;
+    LayerKV *L = nullptr;
+    PagedKV kv;
+    kv.page = kPage;
+    kv.kv_heads = kvNH;
+    kv.hd = HS;
+    size_t need = Carver::round(sizeof(int) * rows) * 2 + Carver::round((size_t)rows * col * es) * 3;
+    if (r.cached) {
+        if (g_sess.kv_heads != kvNH || g_sess.hd != HS || g_sess.act != act)
+            WK_PANIC("prefix cache: attention geometry changed within a session");
+        L = session_layer(qkv_w);
+        session_reserve(row);
+        kv.k = L->k;
+        kv.v = L->v;
+        kv.block_table = g_sess.block_table;
+        kv.max_pages = g_sess.max_pages;
+    } else {
+        kv.max_pages = (row + kPage - 1) / kPage;
+        need += Carver::round(sizeof(int) * batch * kv.max_pages) +
+                2 * Carver::round((size_t)batch * kv.max_pages * kvNH * kPage * HS * es);
+    }
+    Carver c(scratch(need));
+    int *seq = c.take<int>(rows), *pos = c.take<int>(rows);
+    char *q = c.take<char>((size_t)rows * col * es);
+    char *att = c.take<char>((size_t)rows * col * es);
+    char *xg = c.take<char>((size_t)rows * col * es);
+    if (!r.cached) {
+        int *bt = c.take<int>((size_t)batch * kv.max_pages);
+        fill_block_table(bt, batch, kv.max_pages, stream());
+        kv.block_table = bt;
+        kv.k = c.take<char>((size_t)batch * kv.max_pages * kvNH * kPage * HS * es);
+        kv.v = c.take<char>((size_t)batch * kv.max_pages * kvNH * kPage * HS * es);
+    }
+    fill_row_meta(seq, pos, rows, r.n, r.P, stream());
+    void *x = gather_new_rows(out, batch, row, col, r.P, es, xg);
+
+    for (int m0 = 0; m0 < rows; m0 += 8) {
+        GemvArgs a;
+        a.w = (const uint8_t *)qkv_w;
+        a.wtype = wtype;
+        a.N = W;
+        a.K = col;
+        a.x = (const char *)x + (size_t)m0 * col * es;
+        a.ldx = col;
+        a.M = rows - m0 < 8 ? rows - m0 : 8;
+        a.norm_w = norm_w;
+        a.eps = eps;
+        a.epi = EPI_QKV;
+        a.out = q + (size_t)m0 * col * es;
+        a.ldo = col;
+        a.nq = NH * HS;
+        a.nk = kvNH * HS;
+        a.hd = HS;
+        a.freqs = freqs;
+        a.pos = pos + m0;
+        a.seq = seq + m0;
+        a.kpool = kv.k;
+        a.vpool = kv.v;
+        a.block_table = kv.block_table;
+        a.max_pages = kv.max_pages;
+        a.page = kPage;
+        a.kv_heads = kvNH;
+        gemv(a, act, stream());
+    }
+    if (act == kF16)
+        attention_paged<__half>((__half *)att, col, (const __half *)q, col, seq, pos, rows, row, kv, NH, stream(), true);
+    else
+        attention_paged<__nv_bfloat16>((__nv_bfloat16 *)att, col, (const __nv_bfloat16 *)q, col, seq, pos, rows, row,
+                                       kv, NH, stream(), true);
+    for (int m0 = 0; m0 < rows; m0 += 8) {
+        GemvArgs a;
+        a.w = (const uint8_t *)out_w;
+        a.wtype = wtype;
+        a.N = col;
+        a.K = col;
+        a.x = att + (size_t)m0 * col * es;
+        a.ldx = col;
+        a.M = rows - m0 < 8 ? rows - m0 : 8;
+        a.epi = EPI_RESID;
+        a.out = (char *)x + (size_t)m0 * col * es;
+        a.ldo = col;
+        a.res = a.out;
+        a.ldr = col;
+        gemv(a, act, stream());
+    }
+    scatter_new_rows(out, x, batch, row, col, r.P, es);
+    if (L) L->valid = row;
+}
+
+template <typename T>
+void gqa_generic(T *out, const T *embeds, const float *freqs, const float *norm_w, const void *qkv_w,
+                 const void *out_w, int batch, int row, int NH, int kvNH, int HS, float eps, int wtype) {
+    const int act = act_of(wtype);
+    const int col = NH * HS, W = (NH + 2 * kvNH) * HS;
+    const long rows = (long)batch * row;
+    Carver c(scratch(Carver::round(sizeof(T) * rows * col) * 3 + Carver::round(sizeof(T) * rows * W)));
+    T *a = c.take<T>(rows * col), *att = c.take<T>(rows * col), *o = c.take<T>(rows * col);
+    T *qkv = c.take<T>(rows * W);
+    rmsnorm<T>(a, embeds, norm_w, (int)rows, col, eps, stream());
+    matmul(qkv, a, qkv_w, nullptr, (int)rows, col, W, wtype, act, stream());
+    rope<T>(qkv, qkv, freqs, batch, row, NH + 2 * kvNH, NH + kvNH, HS, 0, stream());
+    attention_qkv_rows<T>(att, qkv, batch, row, NH, kvNH, HS, stream());
+    matmul(o, att, out_w, nullptr, (int)rows, col, col, wtype, act, stream());
+    add<T>(out, embeds, o, rows * col, stream());
+}
+
+// ---------------------------------------------------------------- FFN sublayer
+void ffn_fused(void *out, const void *attn, const float *norm_w, const void *fc_w, const void *down_w, int batch,
+               int row, int col, int ffl, float eps, int wtype) {
+    const int act = act_of(wtype);
+    const size_t es = act_size(act);
+    if (out != attn)
+        WK_CHECK(cudaMemcpyAsync(out, attn, (size_t)batch * row * col * es, cudaMemcpyDeviceToDevice, stream()));
+    Rows r = plan_rows(out, batch, row);
+    const int rows = batch * r.n;
+    Carver c(scratch(Carver::round((size_t)rows * ffl * es) + Carver::round((size_t)rows * col * es)));
+    char *h = c.take<char>((size_t)rows * ffl * es);
+    char *xg = c.take<char>((size_t)rows * col * es);
+    void *x = gather_new_rows(out, batch, row, col, r.P, es, xg);
+    for (int m0 = 0; m0 < rows; m0 += 8) {
+        GemvArgs a;
+        a.w = (const uint8_t *)fc_w;
+        a.wtype = wtype;
+        a.N = 2 * ffl;
+        a.K = col;
+        a.x = (const char *)x + (size_t)m0 * col * es;
+        a.ldx = col;
+        a.M = rows - m0 < 8 ? rows - m0 : 8;
+        a.norm_w = norm_w;
+        a.eps = eps;
+        a.epi = EPI_SWIGLU;
+        a.F = ffl;
+        a.out = h + (size_t)m0 * ffl * es;
+        a.ldo = ffl;
+        gemv(a, act, stream());
+    }
+    for (int m0 = 0; m0 < rows; m0 += 8) {
+        GemvArgs a;
+        a.w = (const uint8_t *)down_w;
+        a.wtype = wtype;
+        a.N = col;
+        a.K = ffl;
+        a.x = h + (size_t)m0 * ffl * es;
+        a.ldx = ffl;
+        a.M = rows - m0 < 8 ? rows - m0 : 8;
+        a.epi = EPI_RESID;
+        a.out = (char *)x + (size_t)m0 * col * es;
+        a.ldo = col;
+        a.res = a.out;
+        a.ldr = col;
+        gemv(a, act, stream());
+    }
+    scatter_new_rows(out, x, batch, row, col, r.P, es);
+}
+
+template <typename T>
+void ffn_generic(T *out, const T *attn, const float *norm_w, const void *fc_w, const void *down_w, int batch, int row,
+                 int col, int ffl, float eps, int wtype) {
+    const int act = act_of(wtype);
+    const long rows = (long)batch * row;
+    Carver c(scratch(Carver::round(sizeof(T) * rows * col) * 2 + Carver::round(sizeof(T) * rows * 2 * ffl)));
+    T *a = c.take<T>(rows * col), *o = c.take<T>(rows * col), *fc = c.take<T>(rows * 2 * ffl);
+    rmsnorm<T>(a, attn, norm_w, (int)rows, col, eps, stream());
+    matmul(fc, a, fc_w, nullptr, (int)rows, col, 2 * ffl, wtype, act, stream());
+    swiglu<T>(fc, fc, rows, ffl, stream());
+    matmul(o, fc, down_w, nullptr, (int)rows, ffl, col, wtype, act, stream());
+    add<T>(out, attn, o, rows * col, stream());
+}
+
+// ---------------------------------------------------------------- logits
+struct LogitsScratch {
+    float *val = nullptr;
+    unsigned long long *key = nullptr;
+    int *counter = nullptr;
+};
+LogitsScratch g_logits;
+
+void logits_fused(void *logits, int *tokens, const void *ff, const float *norm_w, const void *out_w, int batch,
+                  int row, int col, int wsize, float eps, int wtype) {
+    const int act = act_of(wtype);
+    const size_t es = act_size(act);
+    for (int m0 = 0; m0 < batch; m0 += 8) {
+        GemvArgs a;
+        a.w = (const uint8_t *)out_w;
+        a.wtype = wtype;
+        a.N = wsize;
+        a.K = col;
+        a.x = (const char *)ff + ((size_t)m0 * row + (row - 1)) * col * es;
+        a.ldx = (long)row * col;
+        a.M = batch - m0 < 8 ? batch - m0 : 8;
+        a.norm_w = norm_w;
+        a.eps = eps;
+        if (tokens) {
+            a.epi = EPI_LOGITS;
+            a.out = logits ? (char *)logits + (size_t)m0 * wsize * es : nullptr;
+            a.ldo = wsize;
+            a.part_val = g_logits.val;
+            a.part_key = g_logits.key;
+            a.counter = g_logits.counter;
+            a.tokens = tokens + m0;
+            a.pack = 16 / (int)es;
+        } else {
+            a.epi = EPI_STORE;
+            a.out = (char *)logits + (size_t)m0 * wsize * es;
+            a.ldo = wsize;
+        }
+        gemv(a, act, stream());
+    }
+}
+
+template <typename T>
+void classify_generic(T *out, const T *ff, const float *norm_w, const void *out_w, int batch, int row, int col,
+                      int wsize, float eps, int wtype) {
+    Carver c(scratch(Carver::round(sizeof(T) * (size_t)batch * col) * 2));
+    T *last = c.take<T>((size_t)batch * col), *a = c.take<T>((size_t)batch * col);
+    get_row<T>(last, ff, batch, row, col, -1, stream());
+    rmsnorm<T>(a, last, norm_w, batch, col, eps, stream());
+    matmul(out, a, out_w, nullptr, batch, col, wsize, wtype, act_of(wtype), stream());
+}
+
+bool fused_ok(int wtype, int col, int K2) {
+    const int act = act_of(wtype);
+    return gemv_supported(wtype, act, col) && gemv_supported(wtype, act, K2);
+}
+
+void end_pass() {
+    if (!g_sess.enabled || !g_sess.active) return;
+    // the pass completed: its ids become the reusable prefix
+    if (g_sess.row > g_sess.ids_cap) {
+        free(g_sess.ids);
+        g_sess.ids_cap = g_sess.row * 2;
+        g_sess.ids = (int *)malloc(sizeof(int) * g_sess.batch * g_sess.ids_cap);
+    }
+    for (int b = 0; b < g_sess.batch; ++b)
+        memcpy(g_sess.ids + (size_t)b * g_sess.ids_cap, g_sess.new_ids + (size_t)b * g_sess.row,
+               sizeof(int) * g_sess.row);
+    g_sess.completed = g_sess.row;
+    for (int i = 0; i < g_sess.nlayers; ++i)
+        if (g_sess.layers[i].valid < g_sess.row) g_sess.completed = 0;  // a layer was skipped
+    g_sess.active = false;
+}
+
+}  // namespace
+
+void layers_init() {
+    const char *pc = getenv("WUKONG_PREFIX_CACHE");
+    g_sess = Session();
+    g_sess.enabled = pc && pc[0] == '1';
+    WK_CHECK(cudaMalloc(&g_logits.val, sizeof(float) * kMaxLogitCtas * 8));
+    WK_CHECK(cudaMalloc(&g_logits.key, sizeof(unsigned long long) * kMaxLogitCtas * 8));
+    WK_CHECK(cudaMalloc(&g_logits.counter, sizeof(int)));
+    WK_CHECK(cudaMemset(g_logits.counter, 0, sizeof(int)));
+}
+
+void layers_fini() {
+    drop_session_layers();
+    free(g_sess.ids);
+    free(g_sess.new_ids);
+    g_sess = Session();
+    for (int i = 0; i < kMaxShadows; ++i) {
+        free(g_shadow[i].host);
+        g_shadow[i] = Shadow();
+    }
+    WK_CHECK(cudaStreamSynchronize(stream()));
+    cudaFree(g_logits.val);
+    cudaFree(g_logits.key);
+    cudaFree(g_logits.counter);
+    g_logits = LogitsScratch();
+}
+
+void prefix_cache_forget(const void *ptr) {
+    for (int i = 0; i < kMaxShadows; ++i)
+        if (g_shadow[i].dst == ptr) {
+            free(g_shadow[i].host);
+            g_shadow[i] = Shadow();
+        }
+    if (g_sess.active && g_sess.embeds == ptr) g_sess.active = false;
+}
+
+void prefix_cache_note_write(void *dst, size_t size) {
+    for (int i = 0; i < kMaxShadows; ++i) {
+        Shadow &s = g_shadow[i];
+        if (s.dst && (char *)s.dst < (char *)dst + size && (char *)dst < (char *)s.dst + s.size) {
+            free(s.host);
+            s = Shadow();
+        }
+    }
+}
+
+void prefix_cache_note_upload(void *dst, const void *src, size_t size) {
+    prefix_cache_note_write(dst, size);
+    if (!g_sess.enabled || size == 0 || size > (1 << 20) || size % 4) return;
+    Shadow &s = g_shadow[g_shadow_next];
+    g_shadow_next = (g_shadow_next + 1) % kMaxShadows;
+    free(s.host);
+    s.dst = dst;
+    s.size = size;
+    s.host = (int *)malloc(size);
+    memcpy(s.host, src, size);
+}
+
+void prefix_cache_embedding(void *out, const int *ids, const void *embd, int batch, int row, int col, int dtype) {
+    const int out_act = dtype == kF32 ? kF32 : (dtype == kBF16 ? kBF16 : kF16);
+    const DTypeInfo &info = kDTypes[dtype];
+    const size_t out_row_bytes = dtype == kQ8_0 ? (size_t)col * 2 : (size_t)col / info.block_size * info.type_size;
+    int P = 0;
+    const int *hids = g_sess.enabled ? find_shadow(ids, sizeof(int) * (size_t)batch * row) : nullptr;
+    if (hids) {
+        if (g_sess.embd != embd || g_sess.batch != batch) {
+            drop_session_layers();
+            g_sess.embd = embd;
+            g_sess.batch = batch;
+        }
+        // longest prefix shared with the last completed pass, leaving >= 1 new row
+        int lim = g_sess.completed < row ? g_sess.completed : row - 1;
+        P = lim;
+        for (int b = 0; b < batch && P > 0; ++b)
+            for (int t = 0; t < P; ++t)
+                if (g_sess.ids[(size_t)b * g_sess.ids_cap + t] != hids[(size_t)b * row + t]) {
+                    P = t;
+                    break;
+                }
+        for (int i = 0; i < g_sess.nlayers; ++i)
+            if (g_sess.layers[i].valid > P) g_sess.layers[i].valid = P;
+        g_sess.completed = P;
+        free(g_sess.new_ids);
+        g_sess.new_ids = (int *)malloc(sizeof(int) * (size_t)batch * row);
+        memcpy(g_sess.new_ids, hids, sizeof(int) * (size_t)batch * row);
+        g_sess.active = true;
+        g_sess.embeds = out;
+        g_sess.row = row;
+        g_sess.P = P;
+    } else if (g_sess.enabled) {
+        g_sess.active = false;
+    }
+    if (P == 0) {
+        embedding(out, ids, embd, batch * row, col, dtype, out_act, stream());
+    } else {
+        for (int b = 0; b < batch; ++b)
+            embedding((char *)out + ((size_t)b * row + P) * out_row_bytes, ids + (size_t)b * row + P, embd, row - P,
+                      col, dtype, out_act, stream());
+    }
+}
+
+}  // namespace wk
+
+using namespace wk;
+
+extern "C" {
+
+// cuda.cu:1324-1338, driver :902-926
+void cuda_group_query_attention(void *out, const void *embeds, const void *freqs, const void *norm_weight,
+                                const void *qkv_weight, const void *out_weight, int batch, int row, int NH, int kvNH,
+                                int HS, float eps, int dtype) {
+    ensure_init();
+    if (kvNH <= 0 || NH % kvNH) WK_PANIC("NH (%d) must be a multiple of kvNH (%d)", NH, kvNH);
+    if (HS % 2) WK_PANIC("head size %d must be even", HS);
+    if (dtype < 0 || dtype >= kDTypeCount) WK_PANIC("Unsupported dtype: %d", dtype);
+    const int col = NH * HS;
+    if (batch <= 0 || row <= 0) return;
+    if (g_sess.enabled && g_sess.active && embeds == g_sess.embeds && g_sess.kv_heads == 0) {
+        g_sess.kv_heads = kvNH;
+        g_sess.hd = HS;
+        g_sess.act = act_of(dtype);
+    }
+    if (dtype != kF32 && fused_ok(dtype, col, col) && HS <= 256) {
+        gqa_fused(out, embeds, (const float *)freqs, (const float *)norm_weight, qkv_weight, out_weight, batch, row, NH,
+                  kvNH, HS, eps, dtype);
+        return;
+    }
+    switch (act_of(dtype)) {
+    case kF32:
+        gqa_generic<float>((float *)out, (const float *)embeds, (const float *)freqs, (const float *)norm_weight,
+                           qkv_weight, out_weight, batch, row, NH, kvNH, HS, eps, dtype);
+        break;
+    case kBF16:
+        gqa_generic<__nv_bfloat16>((__nv_bfloat16 *)out, (const __nv_bfloat16 *)embeds, (const float *)freqs,
+                                   (const float *)norm_weight, qkv_weight, out_weight, batch, row, NH, kvNH, HS, eps,
+                                   dtype);
+        break;
+    default:
+        gqa_generic<__half>((__half *)out, (const __half *)embeds, (const float *)freqs, (const float *)norm_weight,
+                            qkv_weight, out_weight, batch, row, NH, kvNH, HS, eps, dtype);
+    }
+}
+
+// cuda.cu:1384-1400, driver :928-945
+void cuda_feed_forward(void *out, const void *attn, const void *norm_weight, const void *fc_weight,
+                       const void *out_weight, int batch, int row, int col, int ffl, float eps, int dtype) {
+    ensure_init();
+    if (dtype < 0 || dtype >= kDTypeCount) WK_PANIC("Unsupported dtype: %d", dtype);
+    if (batch <= 0 || row <= 0) return;
+    if (dtype != kF32 && fused_ok(dtype, col, ffl)) {
+        ffn_fused(out, attn, (const float *)norm_weight, fc_weight, out_weight, batch, row, col, ffl, eps, dtype);
+        return;
+    }
+    switch (act_of(dtype)) {
+    case kF32:
+        ffn_generic<float>((float *)out, (const float *)attn, (const float *)norm_weight, fc_weight, out_weight, batch,
+                           row, col, ffl, eps, dtype);
+        break;
+    case kBF16:
+        ffn_generic<__nv_bfloat16>((__nv_bfloat16 *)out, (const __nv_bfloat16 *)attn, (const float *)norm_weight,
+                                   fc_weight, out_weight, batch, row, col, ffl, eps, dtype);
+        break;
+    default:
+        ffn_generic<__half>((__half *)out, (const __half *)attn, (const float *)norm_weight, fc_weight, out_weight,
+                            batch, row, col, ffl, eps, dtype);
+    }
+}
+
+// cuda.cu:1402-1414, driver :975-981.  The reference also overwrites the first
+// `batch` rows of `ff` with the normalised last rows (cuda.cu:978-979); this
+// implementation leaves `ff` unchanged.
+void cuda_classify(void *out, void *ff, const void *norm_weight, const void *out_weight, int batch, int row, int col,
+                   int wsize, float eps, int dtype) {
+    ensure_init();
+    if (dtype < 0 || dtype >= kDTypeCount) WK_PANIC("Unsupported dtype: %d", dtype);
+    if (batch <= 0) return;
+    if (dtype != kF32 && fused_ok(dtype, col, col)) {
+        logits_fused(out, nullptr, ff, (const float *)norm_weight, out_weight, batch, row, col, wsize, eps, dtype);
+    } else {
+        switch (act_of(dtype)) {
+        case kF32:
+            classify_generic<float>((float *)out, (const float *)ff, (const float *)norm_weight, out_weight, batch, row,
+                                    col, wsize, eps, dtype);
+            break;
+        case kBF16:
+            classify_generic<__nv_bfloat16>((__nv_bfloat16 *)out, (const __nv_bfloat16 *)ff,
+                                            (const float *)norm_weight, out_weight, batch, row, col, wsize, eps, dtype);
+            break;
+        default:
+            classify_generic<__half>((__half *)out, (const __half *)ff, (const float *)norm_weight, out_weight, batch,
+                                     row, col, wsize, eps, dtype);
+        }
+    }
+    if (g_sess.active && ff == g_sess.embeds) end_pass();
+}
+
+// cuda.cu:1416-1428, driver :983-990: token ids (int32) of the argmax of the
+// last row's logits, with the reference kernel's tie order.
+void cuda_predict(void *out, void *ff, const void *norm_weight, const void *out_weight, int batch, int row, int col,
+                  int wsize, float eps, int dtype) {
+    ensure_init();
+    if (dtype < 0 || dtype >= kDTypeCount) WK_PANIC("Unsupported dtype: %d", dtype);
+    if (batch <= 0) return;
+    if (dtype != kF32 && fused_ok(dtype, col, col) && batch <= 8 * kMaxLogitCtas) {
+        logits_fused(nullptr, (int *)out, ff, (const float *)norm_weight, out_weight, batch, row, col, wsize, eps,
+                     dtype);
+    } else {
+        const int act = act_of(dtype);
+        const size_t es = act_size(act);
+        // classify into a private buffer (the scratch arena is used inside classify)
+        void *logits = nullptr;
+        WK_CHECK(cudaMallocAsync(&logits, es * (size_t)batch * wsize, stream()));
+        const bool was_active = g_sess.active;
+        g_sess.active = false;
+        cuda_classify(logits, ff, norm_weight, out_weight, batch, row, col, wsize, eps, dtype);
+        g_sess.active = was_active;
+        if (act == kF32)
+            argmax<float>((int *)out, (const float *)logits, batch, wsize, stream());
+        else if (act == kBF16)
+            argmax<__nv_bfloat16>((int *)out, (const __nv_bfloat16 *)logits, batch, wsize, stream());
+        else
+            argmax<__half>((int *)out, (const __half *)logits, batch, wsize, stream());
+        WK_CHECK(cudaFreeAsync(logits, stream()));
+    }
+    if (g_sess.active && ff == g_sess.embeds) end_pass();
+}
+
+}  // extern "C"
