@@ -27,7 +27,9 @@ def tol(act):
 
 
 def close(a, b, tol=KAT_TOL):
-    np.testing.assert_allclose(np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel(), rtol=0, atol=tol)
+    # expected values are the reference's float32 literals: compare in float32 terms
+    np.testing.assert_allclose(np.asarray(a, np.float32).astype(np.float64).ravel(),
+                               np.asarray(b, np.float32).astype(np.float64).ravel(), rtol=0, atol=tol)
 
 
 def f32(v):

@@ -148,7 +148,11 @@ void launch_rows(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_r
     if ((int)smem > g_rt.max_smem_optin)
         WK_PANIC("attention: context %d needs %zu B of shared memory", max_len, smem);
     auto kern = attn_rows_kernel<T, KV>;
-    WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    static int configured = 0;
+    if ((int)smem > configured) {
+        WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = (int)smem;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(Hk, nrows);
     cfg.blockDim = dim3(128);
@@ -164,20 +168,286 @@ void launch_rows(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_r
                                 scale));
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core variant for 16-bit paged caches (the decode path).
+//
+// One CTA (4 warps) per (query row, KV head); the G <= 8 query heads of the GQA
+// group are the 8 columns of mma.sync m16n8k16 tiles:
+//   S^T[16 keys x 8 heads] = K[16 keys x D] . Q^T[D x 8 heads]   (A by ldmatrix)
+//   O^T[16 d x 8 heads]    = V^T[16 d x keys] . P^T[keys x 8]     (A by ldmatrix.trans)
+// K and V pages ([page][kv_head][64 tokens][D], 8 or 16 KB contiguous per head)
+// stream through a 4-slot shared-memory ring by 1-D bulk copies; pages that
+// precede the newest token's page were written by earlier launches and are
+// requested before griddepcontrol.wait.  Between the two GEMM passes the
+// softmax runs on the fp16 score row kept in shared memory with the
+// reference's rounding points (see the file header).
+constexpr int kAttnPage = 64;
+constexpr int kAttnSlots = 4;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+template <typename T> struct IsBF16 {
+    static constexpr bool value = false;
+};
+template <> struct IsBF16<__nv_bfloat16> {
+    static constexpr bool value = true;
+};
+
+template <typename T>
+__device__ __forceinline__ void mma16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                      uint32_t b1) {
+    if constexpr (IsBF16<T>::value)
+        mma_bf16(c, a0, a1, a2, a3, b0, b1);
+    else
+        mma_f16(c, a0, a1, a2, a3, b0, b1);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out, long out_rs, const T *__restrict__ q,
+                                                             long q_rs, const int *__restrict__ seq_of_row,
+                                                             const int *__restrict__ pos_of_row, KVPaged kv, int G,
+                                                             int Lpad_max, float scale, int *err, const void *pf,
+                                                             long pf_bytes) {
+    constexpr int kPageBytes = kAttnPage * D * 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *ring = smem;                                                      // [slots][64][D] T
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnSlots * kPageBytes);
+    float *red = reinterpret_cast<float *>(bars + kAttnSlots);                // [8 heads][4 warps]
+    T *qs = reinterpret_cast<T *>(red + 64);                                  // [8][D]
+    T *sc = qs + 8 * D;                                                       // [8][Lpad_max] scores -> P
+
+    const int kvh = blockIdx.x, row = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int seq = seq_of_row[row], pos = pos_of_row[row];
+    const int L = pos + 1;
+    const int npages = (L + kAttnPage - 1) / kAttnPage;
+    const int Lpad = npages * kAttnPage;
+    const T *K = reinterpret_cast<const T *>(kv.k);
+    const T *V = reinterpret_cast<const T *>(kv.v);
+    auto page_src = [&](int i) -> const T * {
+        // units 0..npages-1 are K pages, npages..2*npages-1 the V pages
+        const int p = i < npages ? i : i - npages;
+        const long pg = kv.block_table[(long)seq * kv.max_pages + p];
+        return (i < npages ? K : V) + (pg * kv.kv_heads + kvh) * (long)kAttnPage * D;
+    };
+    if (tid == 64 && pf)
+        l2_prefetch_slice(pf, pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+    if (tid < kAttnSlots) mbar_init(bars + tid, 1);
+    mbar_fence_init();
+    __syncthreads();
+    const int total = 2 * npages;
+    // pages strictly before the newest token's page are complete: fetch them now
+    int issued = 0;
+    if (tid == 0) {
+        for (; issued < kAttnSlots && issued < npages - 1; ++issued) {
+            mbar_expect_tx(bars + issued, kPageBytes);
+            bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (tid == 0) {
+        for (; issued < kAttnSlots && issued < total; ++issued) {
+            mbar_expect_tx(bars + issued, kPageBytes);
+            bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
+        }
+    }
+    // Q of the group, zero-padded to 8 heads
+    const T *qrow = q + (long)row * q_rs + (long)kvh * G * D;
+    for (int i = tid; i < 8 * D; i += 128) qs[i] = i < G * D ? qrow[i] : from_float<T>(0.f);
+    __syncthreads();
+    uint32_t qb[D / 16][2];
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+        qb[kk][0] = *reinterpret_cast<const uint32_t *>(qs + g * D + kk * 16 + 2 * t);
+        qb[kk][1] = *reinterpret_cast<const uint32_t *>(qs + g * D + kk * 16 + 2 * t + 8);
+    }
+
+    // ---- pass 1: scores, rounded to T, and the row max per head
+    float mx0 = -INFINITY, mx1 = -INFINITY;  // heads 2t, 2t+1
+    int consumed = 0;
+    bool ok = true;
+    for (int p = 0; p < npages; ++p, ++consumed) {
+        const int slot = consumed % kAttnSlots;
+        if (!mbar_wait_bounded(bars + slot, (consumed / kAttnSlots) & 1, err, 3)) ok = false;
+        const T *kt = reinterpret_cast<const T *>(ring + slot * kPageBytes) + warp * 16 * D;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ok) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(smem_u32(kt + (lane & 15) * D + kk * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
+                mma16<T>(c, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+            }
+        }
+        // c0, c1: key g, heads 2t, 2t+1; c2, c3: key g + 8
+        const int k0 = p * kAttnPage + warp * 16 + g;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int key = k0 + (i >> 1) * 8, h = 2 * t + (i & 1);
+            const float sv = key < L ? round_to<T>(c[i]) : -INFINITY;
+            if (h < 8) sc[h * Lpad_max + key] = from_float<T>(key < L ? sv : 0.f);
+            if (i & 1)
+                mx1 = fmaxf(mx1, sv * scale);
+            else
+                mx0 = fmaxf(mx0, sv * scale);
+        }
+        __syncthreads();  // everyone is done with this slot
+        if (tid == 0 && issued < total) {
+            const int sl = issued % kAttnSlots;
+            mbar_expect_tx(bars + sl, kPageBytes);
+            bulk_g2s(ring + sl * kPageBytes, page_src(issued), kPageBytes, bars + sl);
+            ++issued;
+        }
+    }
+    // max over the 8 lanes sharing t (g = 0..7), then over warps
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    if (g == 0) {
+        red[(2 * t) * 4 + warp] = mx0;
+        red[(2 * t + 1) * 4 + warp] = mx1;
+    }
+    __syncthreads();
+    // ---- softmax numerators: thread -> (head h, keys j = i, i + 16, ...)
+    const int h = tid >> 4, i0 = tid & 15;  // 8 heads x 16 threads
+    const float M = fmaxf(fmaxf(red[h * 4], red[h * 4 + 1]), fmaxf(red[h * 4 + 2], red[h * 4 + 3]));
+    float lsum = 0.f;
+    for (int j = i0; j < Lpad; j += 16) {
+        float e = 0.f;
+        if (j < L && h < G) {
+            e = expf(to_float(sc[h * Lpad_max + j]) * scale - M);
+            lsum += e;
+        }
+        sc[h * Lpad_max + j] = from_float<T>(e);
+    }
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    const float inv = 1.0f / lsum;
+    for (int j = i0; j < L; j += 16)
+        if (h < G) sc[h * Lpad_max + j] = from_float<T>(to_float(sc[h * Lpad_max + j]) * inv);
+    __syncthreads();
+
+    // ---- pass 2: O^T = V^T . P^T; warp w owns d-tiles w, w + 4
+    constexpr int kDT = D / 16;
+    float o[kDT > 4 ? 2 : 1][4];
+#pragma unroll
+    for (int a = 0; a < (kDT > 4 ? 2 : 1); ++a) o[a][0] = o[a][1] = o[a][2] = o[a][3] = 0.f;
+    for (int p = 0; p < npages; ++p, ++consumed) {
+        const int slot = consumed % kAttnSlots;
+        if (!mbar_wait_bounded(bars + slot, (consumed / kAttnSlots) & 1, err, 3)) ok = false;
+        const T *vt = reinterpret_cast<const T *>(ring + slot * kPageBytes);
+        if (ok) {
+#pragma unroll
+            for (int ks = 0; ks < kAttnPage / 16; ++ks) {
+                const int key0 = p * kAttnPage + ks * 16;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(sc + g * Lpad_max + key0 + 2 * t);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(sc + g * Lpad_max + key0 + 2 * t + 8);
+#pragma unroll
+                for (int a = 0; a < (kDT > 4 ? 2 : 1); ++a) {
+                    const int d0 = (warp + 4 * a) * 16;
+                    if (d0 < D) {
+                        const int mi = lane >> 3, r = lane & 7;
+                        const T *addr = vt + (ks * 16 + r + (mi >> 1) * 8) * D + d0 + (mi & 1) * 8;
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4_t(smem_u32(addr), a0, a1, a2, a3);
+                        mma16<T>(o[a], a0, a1, a2, a3, b0, b1);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && issued < total) {
+            const int sl = issued % kAttnSlots;
+            mbar_expect_tx(bars + sl, kPageBytes);
+            bulk_g2s(ring + sl * kPageBytes, page_src(issued), kPageBytes, bars + sl);
+            ++issued;
+        }
+    }
+    // o[a]: rows d0 + g, d0 + g + 8; columns (heads) 2t, 2t + 1
+    T *orow = out + (long)row * out_rs + (long)kvh * G * D;
+#pragma unroll
+    for (int a = 0; a < (kDT > 4 ? 2 : 1); ++a) {
+        const int d0 = (warp + 4 * a) * 16;
+        if (d0 >= D) continue;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int d = d0 + g + (i >> 1) * 8, hh = 2 * t + (i & 1);
+            if (hh < G) orow[(long)hh * D + d] = from_float<T>(o[a][i]);
+        }
+    }
+}
+
+template <typename T, int D>
+void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
+                      int nrows, int max_len, const KVPaged &kv, int G, cudaStream_t s, bool pdl, const void *pf,
+                      long pf_bytes) {
+    const int Lpad = (max_len + kAttnPage - 1) / kAttnPage * kAttnPage;
+    const size_t smem = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 64 * 4 + 8 * D * 2 +
+                        (size_t)8 * Lpad * 2;
+    if ((int)smem > g_rt.max_smem_optin) WK_PANIC("attention: context %d needs %zu B of shared memory", max_len, smem);
+    auto kern = attn_decode_tc_kernel<T, D>;
+    static int configured = 0;
+    if ((int)smem > configured) {
+        WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = (int)smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kv.kv_heads, nrows);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (pdl && g_rt.pdl) ? 1 : 0;
+    const float scale = 1.0f / sqrtf((float)D);
+    WK_CHECK(cudaLaunchKernelEx(&cfg, kern, out, out_rs, q, q_rs, seq_of_row, pos_of_row, kv, G, Lpad, scale,
+                                g_rt.d_error, pf, pf_bytes));
+}
+
 }  // namespace
 
 template <typename T>
 void attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
-                     int nrows, int max_len, const PagedKV &c, int H, cudaStream_t s, bool pdl) {
+                     int nrows, int max_len, const PagedKV &c, int H, cudaStream_t s, bool pdl, const void *pf,
+                     long pf_bytes) {
     KVPaged kv{c.k, c.v, c.block_table, c.max_pages, c.page, c.kv_heads, c.hd};
+    const int G = H / c.kv_heads;
+    if constexpr (sizeof(T) == 2) {
+        if (c.page == kAttnPage && G <= 8 && (c.hd == 64 || c.hd == 128) && ((uintptr_t)c.k % 16) == 0 &&
+            ((uintptr_t)c.v % 16) == 0) {
+            if (c.hd == 64)
+                launch_decode_tc<T, 64>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows, max_len, kv, G, s, pdl,
+                                        pf, pf_bytes);
+            else
+                launch_decode_tc<T, 128>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows, max_len, kv, G, s, pdl,
+                                         pf, pf_bytes);
+            return;
+        }
+    }
     launch_rows<T>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, 1, nrows, max_len, kv, H, c.kv_heads, c.hd, s, pdl);
 }
 template void attention_paged<__half>(__half *, long, const __half *, long, const int *, const int *, int, int,
-                                      const PagedKV &, int, cudaStream_t, bool);
+                                      const PagedKV &, int, cudaStream_t, bool, const void *, long);
 template void attention_paged<__nv_bfloat16>(__nv_bfloat16 *, long, const __nv_bfloat16 *, long, const int *,
-                                             const int *, int, int, const PagedKV &, int, cudaStream_t, bool);
+                                             const int *, int, int, const PagedKV &, int, cudaStream_t, bool,
+                                             const void *, long);
 template void attention_paged<float>(float *, long, const float *, long, const int *, const int *, int, int,
-                                     const PagedKV &, int, cudaStream_t, bool);
+                                     const PagedKV &, int, cudaStream_t, bool, const void *, long);
 
 // Causal attention straight from fused QKV rows [B, T, (NH + 2 kvNH) HS]
 // (the layout cuda_gq_sdpa takes); out [B, T, NH HS].

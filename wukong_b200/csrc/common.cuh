@@ -58,6 +58,7 @@ struct Runtime {
     int device = -1;
     int num_sms = 0;
     int max_smem_optin = 0;
+    int smem_per_sm = 0;
     cudaStream_t stream = nullptr;
     // device-side error word (mapped pinned memory): bounded waits that give up
     // set a code here
@@ -66,7 +67,8 @@ struct Runtime {
     // grow-only scratch arena for op temporaries (stream ordered on `stream`)
     void *ws = nullptr;
     size_t ws_size = 0;
-    bool pdl = true;  // programmatic dependent launch on the hot kernels
+    bool pdl = true;      // programmatic dependent launch on the hot kernels
+    bool tc_gemm = true;  // tcgen05 GEMM for activation blocks of >= 16 rows
 };
 extern Runtime g_rt;
 
@@ -163,6 +165,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     if (err) atomicCAS(err, 0, code);
     return false;
 }
+// Prefetch this CTA's share of [base, base + bytes) into L2 (fire and forget):
+// the weights of the next kernel in a decode step stream from DRAM while the
+// current kernel is still running.
+__device__ __forceinline__ void l2_prefetch_slice(const void *base, long bytes, int part, int parts) {
+    const long per = ((bytes + parts - 1) / parts + 15) & ~15L;
+    long lo = (long)part * per, hi = lo + per < bytes ? lo + per : bytes;
+    hi &= ~15L;
+    const char *p = (const char *)base;
+    for (long o = lo; o < hi; o += 262144) {
+        const long n = hi - o < 262144 ? hi - o : 262144;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + o), "r"((uint32_t)n) : "memory");
+    }
+}
+
 // 1-D bulk copy global -> shared, completing on `bar` (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(

@@ -109,6 +109,13 @@ __global__ void fill_f32_kernel(float *dst, long n, float v) {
     if (i < n) dst[i] = v;
 }
 
+template <typename T> struct IsHalf {
+    static constexpr bool value = false;
+};
+template <> struct IsHalf<__half> {
+    static constexpr bool value = true;
+};
+
 // token gather converted to the activation type (F32 / F16 / BF16 / Q8_0 tables)
 template <typename T>
 __global__ void embed_kernel(T *__restrict__ out, const int *__restrict__ ids, const uint8_t *__restrict__ table,
@@ -119,6 +126,13 @@ __global__ void embed_kernel(T *__restrict__ out, const int *__restrict__ ids, c
         // an out-of-range id (e.g. -1 from an all-NaN argmax) is reported, never dereferenced
         if (threadIdx.x == 0 && err) atomicCAS(err, 0, 2);
         id = 0;
+    }
+    if (dtype == (sizeof(T) == 2 ? (IsHalf<T>::value ? kF16 : kBF16) : -1) && (col % 8) == 0) {
+        // same 16-bit type: straight 16-byte copies
+        const uint4 *src = reinterpret_cast<const uint4 *>(table + id * col * 2);
+        uint4 *dst = reinterpret_cast<uint4 *>(out + (long)r * col);
+        for (int i = threadIdx.x; i < col / 8; i += blockDim.x) dst[i] = src[i];
+        return;
     }
     for (int i = threadIdx.x; i < col; i += blockDim.x) {
         float v;
@@ -206,8 +220,18 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
     kv.kv_heads = c.n_kv_heads;
     kv.hd = c.head_dim;
     int launches = 0;
+    // L2 prefetch plan: every kernel streams the weights of a later kernel
+    // (qkv -> o, attention -> fc, o -> down, fc -> next qkv, down -> next fc;
+    // the last layer prefetches the head of the logits matrix)
+    auto wbytes = [&](long rows, int K, int wt) -> long {
+        return wt == kQ8_0 ? rows * (K / 32) * 34 : rows * (long)K * 2;
+    };
+    const int W = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+    const long logit_bytes = wbytes(c.vocab, d, c.out_wtype);
+    const long logit_pf = logit_bytes < (48L << 20) ? logit_bytes : (48L << 20);
     for (int l = 0; l < c.n_layers; ++l) {
         const Layer &L = m->layers[l];
+        const bool last = l + 1 == c.n_layers;
         kv.k = m->kpool[l];
         kv.v = m->vpool[l];
         for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
@@ -236,14 +260,19 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.max_pages = kv.max_pages;
             a.page = kPage;
             a.kv_heads = c.n_kv_heads;
+            if (m0 == 0) {
+                a.pf = L.o;
+                a.pf_bytes = wbytes(d, col, c.wtype);
+            }
             gemv(a, m->act, s);
         }
         if (m->act == kF16)
             attention_paged<__half>((__half *)m->att, col, (const __half *)m->q, col, seq, pos, rows, max_len, kv,
-                                    c.n_heads, s, true);
+                                    c.n_heads, s, true, L.fc, wbytes(2L * c.ffn, d, c.wtype));
         else
             attention_paged<__nv_bfloat16>((__nv_bfloat16 *)m->att, col, (const __nv_bfloat16 *)m->q, col, seq, pos,
-                                           rows, max_len, kv, c.n_heads, s, true);
+                                           rows, max_len, kv, c.n_heads, s, true, L.fc,
+                                           wbytes(2L * c.ffn, d, c.wtype));
         ++launches;
         for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
             GemvArgs a;
@@ -259,6 +288,10 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.ldo = d;
             a.res = a.out;
             a.ldr = d;
+            if (m0 == 0) {
+                a.pf = L.down;
+                a.pf_bytes = wbytes(d, c.ffn, c.wtype);
+            }
             gemv(a, m->act, s);
         }
         for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
@@ -276,6 +309,10 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.F = c.ffn;
             a.out = (char *)m->h + (size_t)m0 * c.ffn * es;
             a.ldo = c.ffn;
+            if (m0 == 0) {
+                a.pf = last ? (const void *)m->out_w : (const void *)m->layers[l + 1].qkv;
+                a.pf_bytes = last ? logit_pf / 2 : wbytes(W, d, c.wtype);
+            }
             gemv(a, m->act, s);
         }
         for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
@@ -292,6 +329,10 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.ldo = d;
             a.res = a.out;
             a.ldr = d;
+            if (m0 == 0) {
+                a.pf = last ? (const char *)m->out_w + logit_pf / 2 : (const void *)m->layers[l + 1].fc;
+                a.pf_bytes = last ? logit_pf / 2 : wbytes(2L * c.ffn, d, c.wtype);
+            }
             gemv(a, m->act, s);
         }
     }

@@ -1,0 +1,468 @@
+// tcgen05 / TMEM GEMM with the Q8_0 dequantisation fused into the A-operand
+// load, for prefill and batched decode (activation rows M >= 16).
+//
+//   D[128 weight rows x BN tokens] (fp32, TMEM) = W_tile[128 x K] . X_tile[BN x K]^T
+//
+// Reference semantics (cuda.cu:1095-1111, :270-341): W is dequantised to half
+// exactly as the reference does (w = (half)(float(scale) * q)), multiplied with
+// half activations, accumulated in fp32 and rounded once to half at the store.
+//
+// CTA = 6 warps, one output tile per CTA:
+//   warp 0 (lane 0)  TMA producer: raw Q8_0 tiles (128 rows x 256 k = 128 x 272 B,
+//                    one 2-D box) and activation tiles (BN rows x 64 k, 128-byte
+//                    swizzle); for 16-bit weights also the A tiles.
+//   warp 1           allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN,
+//                    K=16 per instruction) and tcgen05.commit.
+//   warps 2..5       one thread per weight row: read the raw row from shared
+//                    memory (conflict-free 16-byte loads), dequantise in registers
+//                    (byte-permute -> exact half2, half2 multiply by the scale) and
+//                    write the 128-byte-swizzled fp16 A tile the UMMA descriptor
+//                    expects; after the K loop they drain TMEM (tcgen05.ld) and run
+//                    the fused epilogue (store+bias, residual, RoPE+KV append,
+//                    SwiGLU pairing of up/gate rows).
+// Every mbarrier wait is bounded (one second); a wait that gives up records an
+// error code and the CTA runs to completion without further waiting.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "wukong_internal.cuh"
+
+namespace wk {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kASlots = 4;                      // 64-k operand stages
+constexpr int kRawSlots = 2;                    // 256-k raw Q8_0 stages
+constexpr int kATileBytes = 128 * 128;          // 128 rows x 64 halves
+constexpr int kRawBytes = 128 * 272;            // 128 rows x 8 Q8_0 blocks
+constexpr int kKB = 256;                        // k per raw stage
+
+// ---------------------------------------------------------------- PTX
+__device__ __forceinline__ void tma2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor: K-major operand in the canonical 128-byte
+// swizzle layout (rows of 128 bytes, 8-row groups 1024 bytes apart).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address
+    d |= (uint64_t)1 << 16;                             // leading byte offset (unused for this layout)
+    d |= (uint64_t)(1024 >> 4) << 32;                   // stride byte offset: next 8-row group
+    d |= (uint64_t)1 << 46;                             // descriptor version
+    d |= (uint64_t)2 << 61;                             // 128-byte swizzle
+    return d;
+}
+
+struct Bars {
+    uint64_t raw_full[kRawSlots], raw_empty[kRawSlots];
+    uint64_t a_full[kASlots], b_full[kASlots], ab_empty[kASlots];
+    uint64_t acc_full;
+    uint32_t tmem;
+};
+
+template <int BN> struct Layout {
+    static constexpr int kBTile = BN * 128;
+    static constexpr size_t kA = 0;
+    static constexpr size_t kB = kA + (size_t)kASlots * kATileBytes;
+    static constexpr size_t kRaw = kB + (size_t)kASlots * kBTile;
+    static constexpr size_t kBars = kRaw + (size_t)kRawSlots * kRawBytes;
+    static constexpr size_t kTotal = kBars + sizeof(Bars) + 1024;  // + alignment slack
+};
+
+// Dequantise 64 k (Q8_0 blocks 2j, 2j+1 of this row's 272 raw bytes held in
+// `w`, 68 words) into the 128-byte swizzled A row.
+__device__ __forceinline__ void dequant_sub(const uint32_t (&w)[68], int j, uint8_t *arow, int row) {
+#pragma unroll
+    for (int bb = 0; bb < 2; ++bb) {
+        const int b = 2 * j + bb;  // compile-time after unrolling j
+        const int off = 34 * b;    // byte offset of the block
+        // scale: bytes off, off+1
+        const uint32_t sw = w[off >> 2];
+        const uint32_t sbits = (off & 2) ? (sw >> 16) : (sw & 0xffffu);
+        const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)sbits));
+        // 32 quants start at off + 2: 8 words, realigned when off + 2 is not 4-aligned
+        uint32_t q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int byte = off + 2 + 4 * i;
+            if (byte & 2)
+                q[i] = __byte_perm(w[byte >> 2], w[(byte >> 2) + 1], 0x5432);
+            else
+                q[i] = w[byte >> 2];
+        }
+        // 32 halves = 4 x 16-byte chunks (chunk c covers k = 8c .. 8c+7 of the 64-k sub-tile)
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            __half2 h[4];
+            i8x4_to_h2x2(q[2 * cc], h[0], h[1]);
+            i8x4_to_h2x2(q[2 * cc + 1], h[2], h[3]);
+            uint4 v;
+            v.x = h2_as_u32(__hmul2(h[0], s2));
+            v.y = h2_as_u32(__hmul2(h[1], s2));
+            v.z = h2_as_u32(__hmul2(h[2], s2));
+            v.w = h2_as_u32(__hmul2(h[3], s2));
+            const int c = bb * 4 + cc;
+            *reinterpret_cast<uint4 *>(arow + ((c ^ (row & 7)) << 4)) = v;
+        }
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_out(const GemmArgs &a, int n, int m, float acc, const float *partner) {
+    // partner: value of the paired row (RoPE: n ^ 1, SwiGLU: the gate row)
+    switch (a.epi) {
+    case EPI_STORE: {
+        if (a.bias) acc += to_float(reinterpret_cast<const T *>(a.bias)[n]);
+        reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(acc);
+        break;
+    }
+    case EPI_RESID: {
+        const float y = round_to<T>(acc);
+        const float rv = to_float(reinterpret_cast<const T *>(a.res)[(long)m * a.ldr + n]);
+        reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(rv + y);
+        break;
+    }
+    case EPI_QKV: {
+        const float y = round_to<T>(acc);
+        const int pos = a.pos[m];
+        if (n < a.nq + a.nk) {
+            const float yp = round_to<T>(*partner);
+            const int dd = (n - (n < a.nq ? 0 : a.nq)) % a.hd;
+            const float *f = a.freqs + (long)pos * a.hd + (dd & ~1);
+            const float cs = f[0], sn = f[1];
+            const float o = (n & 1) ? (yp * sn + y * cs) : (y * cs - yp * sn);
+            if (n < a.nq) {
+                reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(o);
+            } else {
+                const int kh = (n - a.nq) / a.hd;
+                const long page = a.block_table[(long)a.seq[m] * a.max_pages + pos / a.page];
+                reinterpret_cast<T *>(a.kpool)[((page * a.kv_heads + kh) * a.page + pos % a.page) * a.hd + dd] =
+                    from_float<T>(o);
+            }
+        } else {
+            const int dd = (n - a.nq - a.nk) % a.hd, vh = (n - a.nq - a.nk) / a.hd;
+            const long page = a.block_table[(long)a.seq[m] * a.max_pages + pos / a.page];
+            reinterpret_cast<T *>(a.vpool)[((page * a.kv_heads + vh) * a.page + pos % a.page) * a.hd + dd] =
+                from_float<T>(y);
+        }
+        break;
+    }
+    case EPI_SWIGLU: {
+        const float u = round_to<T>(acc);
+        const float g = round_to<T>(*partner);
+        const float sig = 1.0f / (1.0f + expf(-g));
+        reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>((g * sig) * u);
+        break;
+    }
+    default:
+        break;
+    }
+}
+
+template <typename T, int WT, int BN>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
+    using L = Layout<BN>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled tiles
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *A = smem + L::kA;
+    uint8_t *B = smem + L::kB;
+    uint8_t *RAW = smem + L::kRaw;
+    Bars *bars = reinterpret_cast<Bars *>(smem + L::kBars);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tile = blockIdx.x, m0 = blockIdx.y * BN;
+    const bool swiglu = a.epi == EPI_SWIGLU;
+    const int nkb = a.K / kKB;      // raw stages (Q8_0) / 4 x 64-k subs
+    const int nsub = a.K / 64;      // operand stages
+    constexpr bool kQ8 = WT == kQ8_0;
+    constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+    constexpr uint32_t kIdesc = (1u << 4) | ((WT == kBF16 ? 1u : 0u) << 7) | ((WT == kBF16 ? 1u : 0u) << 10) |
+                                ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRawSlots; ++i) {
+            mbar_init(&bars->raw_full[i], 1);
+            mbar_init(&bars->raw_empty[i], 128);
+        }
+        for (int i = 0; i < kASlots; ++i) {
+            mbar_init(&bars->a_full[i], kQ8 ? 128 : 1);
+            mbar_init(&bars->b_full[i], 1);
+            mbar_init(&bars->ab_empty[i], 1);
+        }
+        mbar_init(&bars->acc_full, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) tc_alloc(&bars->tmem, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem;
+    int *err = a.err;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // weights do not depend on the previous kernel: start them first
+            const int wy = swiglu ? n_tile * 64 : n_tile * 128;
+            auto issue_raw = [&](int kb) {
+                const int s = kb % kRawSlots;
+                mbar_expect_tx(&bars->raw_full[s], kRawBytes);
+                if (swiglu) {
+                    tma2d(RAW + (size_t)s * kRawBytes, &a.wmap, kb * 136, wy, &bars->raw_full[s]);
+                    tma2d(RAW + (size_t)s * kRawBytes + 64 * 272, &a.wmap, kb * 136, a.F + wy, &bars->raw_full[s]);
+                } else {
+                    tma2d(RAW + (size_t)s * kRawBytes, &a.wmap, kb * 136, wy, &bars->raw_full[s]);
+                }
+            };
+            int raw_issued = 0;
+            if (kQ8)
+                for (; raw_issued < kRawSlots && raw_issued < nkb; ++raw_issued) issue_raw(raw_issued);
+            pdl_wait();
+            for (int i = 0; i < nsub && ok; ++i) {
+                const int s = i % kASlots;
+                if (i >= kASlots && !mbar_wait_bounded(&bars->ab_empty[s], ((i / kASlots) - 1) & 1, err, 10)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t tx = (uint32_t)(L::kBTile + (kQ8 ? 0 : kATileBytes));
+                mbar_expect_tx(&bars->b_full[s], tx);
+                tma2d(B + (size_t)s * L::kBTile, &a.xmap, i * 64, m0, &bars->b_full[s]);
+                if (!kQ8) {
+                    if (swiglu) {
+                        tma2d(A + (size_t)s * kATileBytes, &a.wmap, i * 64, wy, &bars->b_full[s]);
+                        tma2d(A + (size_t)s * kATileBytes + 64 * 128, &a.wmap, i * 64, a.F + wy, &bars->b_full[s]);
+                    } else {
+                        tma2d(A + (size_t)s * kATileBytes, &a.wmap, i * 64, wy, &bars->b_full[s]);
+                    }
+                }
+                // keep the raw ring one stage ahead of the operand stages
+                if (kQ8 && (i % 4) == 3 && raw_issued < nkb) {
+                    const int kb = raw_issued;
+                    if (!mbar_wait_bounded(&bars->raw_empty[kb % kRawSlots], ((kb / kRawSlots) - 1) & 1, err, 11)) {
+                        ok = false;
+                        break;
+                    }
+                    issue_raw(kb);
+                    ++raw_issued;
+                }
+            }
+        }
+        pdl_trigger();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            pdl_wait();
+            for (int i = 0; i < nsub && ok; ++i) {
+                const int s = i % kASlots;
+                const uint32_t par = (i / kASlots) & 1;
+                if (!mbar_wait_bounded(&bars->b_full[s], par, err, 12)) ok = false;
+                if (kQ8 && ok && !mbar_wait_bounded(&bars->a_full[s], par, err, 13)) ok = false;
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t abase = smem_u32(A + (size_t)s * kATileBytes);
+                const uint32_t bbase = smem_u32(B + (size_t)s * L::kBTile);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc_mma(tmem, sw128_desc(abase + 32 * kk), sw128_desc(bbase + 32 * kk), kIdesc, (i | kk) != 0);
+                tc_commit(&bars->ab_empty[s]);
+            }
+            tc_commit(&bars->acc_full);
+        }
+        pdl_trigger();
+    } else {
+        // warps 2..5: row = TMEM lane quarter (warp % 4) * 32 + lane
+        const int row = (warp & 3) * 32 + lane;
+        pdl_trigger();
+        if (kQ8) {
+            for (int kb = 0; kb < nkb && ok; ++kb) {
+                const int rs = kb % kRawSlots;
+                if (!mbar_wait_bounded(&bars->raw_full[rs], (kb / kRawSlots) & 1, err, 14)) {
+                    ok = false;
+                    break;
+                }
+                uint32_t w[68];
+                const uint4 *src = reinterpret_cast<const uint4 *>(RAW + (size_t)rs * kRawBytes + row * 272);
+#pragma unroll
+                for (int i = 0; i < 17; ++i) {
+                    const uint4 v = src[i];
+                    w[4 * i] = v.x;
+                    w[4 * i + 1] = v.y;
+                    w[4 * i + 2] = v.z;
+                    w[4 * i + 3] = v.w;
+                }
+                mbar_arrive(&bars->raw_empty[rs]);  // the raw row is in registers
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int i = kb * 4 + j;
+                    const int s = i % kASlots;
+                    if (i >= kASlots && !mbar_wait_bounded(&bars->ab_empty[s], ((i / kASlots) - 1) & 1, err, 15)) {
+                        ok = false;
+                        break;
+                    }
+                    dequant_sub(w, j, A + (size_t)s * kATileBytes + row * 128, row);
+                    fence_proxy_async();  // generic-proxy writes -> visible to tcgen05.mma
+                    mbar_arrive(&bars->a_full[s]);
+                }
+            }
+        }
+        // epilogue: TMEM -> registers -> fused store (reads residual / positions
+        // written by earlier kernels)
+        pdl_wait();
+        const bool acc_ok = ok && mbar_wait_bounded(&bars->acc_full, 0, err, 16);
+        tc_fence_after();
+        float *xchg = reinterpret_cast<float *>(RAW);  // [128 rows][32 columns] for row pairing
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t v[32];
+            const uint32_t taddr = tmem + (((uint32_t)(warp & 3) * 32) << 16) + (uint32_t)c0;
+            tc_ld32(taddr, v);
+            if (!acc_ok)
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0u;
+            // pairing partner (RoPE: row ^ 1 in the neighbouring lane; SwiGLU: row + 64)
+            if (swiglu) {
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+                for (int i = 0; i < 32; ++i) xchg[row * 33 + i] = __uint_as_float(v[i]);
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+            }
+            const int n = swiglu ? (n_tile * 64 + row) : (n_tile * 128 + row);
+            const bool row_ok = swiglu ? (row < 64 && n < a.F) : (n < a.N);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int m = m0 + c0 + i;
+                float pv = 0.f;
+                if (a.epi == EPI_QKV) pv = __shfl_xor_sync(0xffffffffu, __uint_as_float(v[i]), 1);
+                if (swiglu && row < 64) pv = xchg[(row + 64) * 33 + i];
+                if (row_ok && m < a.M) store_out<T>(a, n, m, __uint_as_float(v[i]), &pv);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tc_dealloc(tmem, kTmemCols);
+    }
+}
+
+template <typename T, int WT, int BN> void launch_tc(const GemmArgs &a, cudaStream_t s, bool pdl) {
+    auto kern = gemm_tc_kernel<T, WT, BN>;
+    const size_t smem = Layout<BN>::kTotal;
+    static bool configured = false;
+    if (!configured) {
+        WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = true;
+    }
+    const int ntiles = a.epi == EPI_SWIGLU ? (a.F + 63) / 64 : (a.N + 127) / 128;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ntiles, (a.M + BN - 1) / BN);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    WK_CHECK(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int wtype, int act, int K, int N, int epi, int F) {
+    if (act == kF32) return false;
+    if (wtype == kQ8_0 && (act != kF16 || K % kKB)) return false;
+    if ((wtype == kF16 && act != kF16) || (wtype == kBF16 && act != kBF16)) return false;
+    if (wtype != kQ8_0 && wtype != kF16 && wtype != kBF16) return false;
+    if (K % 64) return false;
+    if (epi == EPI_SWIGLU && F % 64) return false;
+    if (epi == EPI_LOGITS) return false;
+    (void)N;
+    return true;
+}
+
+void gemm_tc(GemmArgs a, int act, cudaStream_t s) {
+    if (!gemm_tc_supported(a.wtype, act, a.K, a.N, a.epi, a.F)) WK_PANIC("gemm_tc: unsupported problem");
+    if (!a.err) a.err = g_rt.d_error;
+    const size_t es = 2;
+    // activations: [M rows][K] with row stride ldx, boxes of 64 k x BN rows, 128-byte swizzle
+    const int BN = a.M >= 96 ? 128 : (a.M >= 48 ? 64 : 32);
+    if (((uintptr_t)a.x % 16) || ((a.ldx * es) % 16)) WK_PANIC("gemm_tc: activations must be 16-byte aligned rows");
+    if (!encode_map_2d(&a.xmap, a.x, act == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                       (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.ldx * es, 64, (uint32_t)BN,
+                       CU_TENSOR_MAP_SWIZZLE_128B))
+        WK_PANIC("gemm_tc: activation tensor map");
+    const long rows = a.epi == EPI_SWIGLU ? 2L * a.F : (long)a.N;
+    const int box_rows = a.epi == EPI_SWIGLU ? 64 : 128;
+    if (a.wtype == kQ8_0) {
+        const CUtensorMap *m = weight_map(a.w, rows, (long)(a.K / 32) * 34, 136, box_rows);
+        if (!m) WK_PANIC("gemm_tc: weight rows are not 16-byte aligned");
+        a.wmap = *m;
+    } else {
+        if (((uintptr_t)a.w % 16) || !encode_map_2d(&a.wmap, a.w,
+                                                     a.wtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                                     (uint64_t)a.K, (uint64_t)rows, (uint64_t)a.K * 2, 64,
+                                                     (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
+            WK_PANIC("gemm_tc: weight tensor map");
+    }
+    const bool pdl = g_rt.pdl && a.pdl;
+#define WK_TC_LAUNCH(T, W)                        \
+    do {                                          \
+        if (BN == 128)                            \
+            launch_tc<T, W, 128>(a, s, pdl);      \
+        else if (BN == 64)                        \
+            launch_tc<T, W, 64>(a, s, pdl);       \
+        else                                      \
+            launch_tc<T, W, 32>(a, s, pdl);       \
+    } while (0)
+    if (a.wtype == kQ8_0)
+        WK_TC_LAUNCH(__half, kQ8_0);
+    else if (a.wtype == kF16)
+        WK_TC_LAUNCH(__half, kF16);
+    else
+        WK_TC_LAUNCH(__nv_bfloat16, kBF16);
+#undef WK_TC_LAUNCH
+}
+
+}  // namespace wk

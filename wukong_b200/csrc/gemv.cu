@@ -5,13 +5,14 @@
 // activations with fp32 accumulation and one rounding to T at the store.
 //
 // Design (B200):
-//  * A CTA of 4 warps owns 16-row weight tiles (grid-stride).  Each warp streams
+//  * A CTA of 8 warps owns 16-row weight tiles (grid-stride).  Each warp streams
 //    its share of the tile's K-chunks (256 Q8_0 values = 272 B per row, or 128
-//    16-bit values = 256 B per row) with 1-D bulk copies (cp.async.bulk, one per
-//    row, 16 lanes in parallel) into a private 4-stage shared-memory ring
-//    guarded by mbarriers.  The first stages are requested before
-//    griddepcontrol.wait, so weight streaming overlaps the tail of the
-//    producing kernel under programmatic dependent launch.
+//    16-bit values = 256 B per row) into a private 3-stage shared-memory ring
+//    with 16-byte cp.async copies: every lane moves one 16-byte piece per
+//    instruction, so each instruction is a fully coalesced 512-byte request.
+//    The first stages are requested before griddepcontrol.wait, so weight
+//    streaming overlaps the tail of the producing kernel under programmatic
+//    dependent launch.
 //  * Dequantisation happens in registers: four int8 quants become two exact
 //    half2 by a byte-permute/subtract, then one half2 multiply by the block
 //    scale gives exactly the reference's rounded fp16 weights.
@@ -31,33 +32,49 @@ namespace wk {
 
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kStages = 4;
+constexpr int kWarps = 8;
+constexpr int kStages = 3;
+constexpr size_t kXStageMax = 32 * 1024;  // X is staged in shared memory up to this size
 constexpr int kTileRows = 16;
-constexpr int kRowBytesMax = 272;  // per-row bytes of one stage (Q8_0: 8 blocks)
+constexpr int kStageBytes = kTileRows * 272;  // one unit: 16 rows x (8 Q8_0 blocks | 128 halves)
 
 template <int WT> struct WFmt;
 template <> struct WFmt<kQ8_0> {
-    static constexpr int kChunk = 256;          // elements per row per stage
-    static constexpr int kChunkBytes = 272;     // 8 blocks * 34
+    static constexpr int kChunk = 256;  // elements per row per stage
+    static constexpr int kRowB = 272;   // bytes per row per stage (8 blocks)
     static __host__ __device__ long row_bytes(int K) { return (long)(K / 32) * 34; }
     static __host__ __device__ int chunk_bytes(int elems) { return elems / 32 * 34; }
 };
 template <> struct WFmt<kF16> {
     static constexpr int kChunk = 128;
-    static constexpr int kChunkBytes = 256;
+    static constexpr int kRowB = 256;
     static __host__ __device__ long row_bytes(int K) { return (long)K * 2; }
     static __host__ __device__ int chunk_bytes(int elems) { return elems * 2; }
 };
 template <> struct WFmt<kBF16> : WFmt<kF16> {};
 
 struct Smem {
-    uint8_t *ring;   // [kWarps][kStages][16][kRowBytesMax]
-    uint64_t *bars;  // [kWarps][kStages]
-    uint2 *xs;       // [Kpad/16][M][4] x 4 values (8 bytes)
-    float *red;      // [kWarps][16][8]
-    float *misc;     // norm scales [8], logits partials
+    uint8_t *ring;    // [kWarps][kStages][16][kRowB]
+    uint64_t *bars;   // [kWarps][kStages] TMA completion
+    // X as the MMA B operand: row-major [M][ld] 16-bit values viewed as uint2.
+    // Lane (g, t) of k-slice s reads the 4 values at k = 16 s + 4 t of row g,
+    // i.e. uint2 (4 s + t), which matches the A-side k permutation.  Points to
+    // global memory, or to shared memory when an RMSNorm prologue is fused.
+    const uint2 *xsrc;
+    long xld;       // row stride in uint2
+    uint2 *xn;      // [M][Kpad / 4] normalised X (RMSNorm prologue only)
+    float *red;     // [kWarps][16][8]
+    float *misc;    // norm scales [8], logits partials [128] + keys [128]
 };
+
+// 2-D TMA tile load into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
 
 __device__ __forceinline__ int tile_row(const GemvArgs &a, int tile, int r) {
     if (a.epi == EPI_SWIGLU) return r < 8 ? tile * 8 + r : a.F + tile * 8 + (r - 8);
@@ -72,105 +89,142 @@ __device__ __forceinline__ bool row_valid(const GemvArgs &a, int tile, int r) {
 }
 
 // Request the bytes of one (tile, chunk) unit into ring slot `slot` of warp `w`.
+// TMA path: lane 0 issues one 2-D box of 16 rows (two boxes of 8 rows for the
+// up|gate pairing of SwiGLU); rows past N arrive zero-filled.  Otherwise (rows
+// that are not 16-byte aligned) a synchronous copy by the warp, zero padded.
 template <int WT>
 __device__ __forceinline__ void issue_unit(const GemvArgs &a, const Smem &sm, int w, int slot, int tile, int chunk,
-                                           int lane, bool bulk) {
+                                           int lane, bool tma) {
     using F = WFmt<WT>;
-    const long rb = F::row_bytes(a.K);
     const int e0 = chunk * F::kChunk;
-    const int elems = min(F::kChunk, a.K - e0);
-    const int bytes = F::chunk_bytes(elems);
-    uint8_t *dst0 = sm.ring + ((size_t)(w * kStages + slot) * kTileRows) * kRowBytesMax;
-    uint64_t *bar = sm.bars + w * kStages + slot;
-    if (bulk) {
-        int nvalid = 0;
-#pragma unroll 4
-        for (int r = 0; r < kTileRows; ++r) nvalid += row_valid(a, tile, r) ? 1 : 0;
-        if (lane == 0) mbar_expect_tx(bar, (uint32_t)(nvalid * bytes));
-        __syncwarp();
-        if (lane < kTileRows && row_valid(a, tile, lane)) {
-            const uint8_t *src = a.w + (long)tile_row(a, tile, lane) * rb + F::chunk_bytes(e0);
-            bulk_g2s(dst0 + lane * kRowBytesMax, src, (uint32_t)bytes, bar);
+    uint8_t *dst0 = sm.ring + (size_t)(w * kStages + slot) * kStageBytes;
+    if (tma) {
+        if (lane == 0) {
+            uint64_t *bar = sm.bars + w * kStages + slot;
+            mbar_expect_tx(bar, kTileRows * F::kRowB);
+            const int x = F::chunk_bytes(e0) / 2;  // uint16 column of the box
+            if (a.epi == EPI_SWIGLU) {
+                tma_load_2d(dst0, &a.wmap, x, tile * 8, bar);
+                tma_load_2d(dst0 + 8 * F::kRowB, &a.wmap, x, a.F + tile * 8, bar);
+            } else {
+                tma_load_2d(dst0, &a.wmap, x, tile * kTileRows, bar);
+            }
         }
     } else {
-        // unaligned rows: synchronous copy by the warp, zero padding to a 16-slice
+        const long rb = F::row_bytes(a.K);
+        const int elems = min(F::kChunk, a.K - e0);
+        const int bytes = F::chunk_bytes(elems);
         const int padded = F::chunk_bytes(((elems + 15) / 16) * 16);
         for (int r = 0; r < kTileRows; ++r) {
             const bool ok = row_valid(a, tile, r);
             const uint8_t *src = ok ? a.w + (long)tile_row(a, tile, r) * rb + F::chunk_bytes(e0) : nullptr;
-            for (int i = lane; i < padded; i += 32) dst0[r * kRowBytesMax + i] = (ok && i < bytes) ? src[i] : 0;
+            for (int i = lane; i < padded; i += 32) dst0[r * F::kRowB + i] = (ok && i < bytes) ? src[i] : 0;
         }
-        __syncwarp();
     }
 }
 
-// Consume one unit: accumulate the 16 x 8 tile over the chunk's k-slices.
+// Issue the next unit of this warp's sequence into `slot`.
+template <int WT>
+__device__ __forceinline__ void produce_unit(const GemvArgs &a, const Smem &sm, int w, int slot, int lane,
+                                             bool has_work, int ntiles, int nchunks, int &p_tile, int &p_chunk) {
+    if (has_work && p_tile < ntiles) {
+        issue_unit<WT>(a, sm, w, slot, p_tile, p_chunk, lane, true);
+        p_chunk += kWarps;
+        if (p_chunk >= nchunks) {
+            p_chunk = w;
+            p_tile += gridDim.x;
+        }
+    }
+}
+
+// One Q8_0 block (32 k, two MMA k-slices) of rows g and g + 8 of the staged tile:
+// lane t takes quant bytes 4t..4t+3 of each 16-value half.  Odd blocks start
+// their quants 4-byte aligned (34 * odd + 2 = 0 mod 4); even ones are realigned
+// by a byte permute of two neighbouring words.
+__device__ __forceinline__ void q8_block(const uint8_t *r0, const uint8_t *r1, int off, bool odd, int t, uint2 x0,
+                                         uint2 x1, float (&c)[2][4]) {
+    const __half2 s0 = __half2half2(*reinterpret_cast<const __half *>(r0 + off));
+    const __half2 s1 = __half2half2(*reinterpret_cast<const __half *>(r1 + off));
+    uint32_t q0[2], q1[2];  // [slice] quant words for rows g, g+8
+    if (odd) {
+        q0[0] = *reinterpret_cast<const uint32_t *>(r0 + off + 2 + 4 * t);
+        q0[1] = *reinterpret_cast<const uint32_t *>(r0 + off + 18 + 4 * t);
+        q1[0] = *reinterpret_cast<const uint32_t *>(r1 + off + 2 + 4 * t);
+        q1[1] = *reinterpret_cast<const uint32_t *>(r1 + off + 18 + 4 * t);
+    } else {
+        const uint32_t *p0 = reinterpret_cast<const uint32_t *>(r0 + off + 4 * t);
+        const uint32_t *p1 = reinterpret_cast<const uint32_t *>(r1 + off + 4 * t);
+        q0[0] = __byte_perm(p0[0], p0[1], 0x5432);
+        q0[1] = __byte_perm(p0[4], p0[5], 0x5432);
+        q1[0] = __byte_perm(p1[0], p1[1], 0x5432);
+        q1[1] = __byte_perm(p1[4], p1[5], 0x5432);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        __half2 lo0, hi0, lo1, hi1;
+        i8x4_to_h2x2(q0[h], lo0, hi0);
+        i8x4_to_h2x2(q1[h], lo1, hi1);
+        const uint32_t a0 = h2_as_u32(__hmul2(lo0, s0)), a2 = h2_as_u32(__hmul2(hi0, s0));
+        const uint32_t a1 = h2_as_u32(__hmul2(lo1, s1)), a3 = h2_as_u32(__hmul2(hi1, s1));
+        const uint2 xv = h ? x1 : x0;
+        mma_f16(c[h], a0, a1, a2, a3, xv.x, xv.y);
+    }
+}
+
+// Consume one unit: accumulate the 16 x 8 tile over the chunk's k-slices into
+// two independent accumulators (even / odd slice) to halve the MMA chain.
 template <int WT>
 __device__ __forceinline__ void consume_unit(const GemvArgs &a, const Smem &sm, int w, int slot, int chunk, int lane,
-                                             float (&c)[4]) {
+                                             float (&c)[2][4]) {
     using F = WFmt<WT>;
     const int g = lane >> 2, t = lane & 3;
     const int e0 = chunk * F::kChunk;
     const int elems = min(F::kChunk, a.K - e0);
-    const uint8_t *st = sm.ring + ((size_t)(w * kStages + slot) * kTileRows) * kRowBytesMax;
-    const uint8_t *r0 = st + g * kRowBytesMax;
-    const uint8_t *r1 = st + (g + 8) * kRowBytesMax;
+    const uint8_t *st = sm.ring + (size_t)(w * kStages + slot) * kStageBytes;
+    const uint8_t *r0 = st + g * F::kRowB;
+    const uint8_t *r1 = st + (g + 8) * F::kRowB;
     const int M = a.M;
-    const int s_base = e0 / 16;
+    const bool has_x = g < M;
+    const uint2 *xl = sm.xsrc + (has_x ? g : 0) * sm.xld + (e0 / 16) * 4 + t;  // slice e0/16 of row g
+    constexpr int xstep = 4;                                                   // uint2 per slice
     if constexpr (WT == kQ8_0) {
         const int nblk = elems / 32;
-#pragma unroll 2
-        for (int b = 0; b < nblk; ++b) {
-            const int off = b * 34;
-            const __half2 s0 = __half2half2(*reinterpret_cast<const __half *>(r0 + off));
-            const __half2 s1 = __half2half2(*reinterpret_cast<const __half *>(r1 + off));
-            uint32_t q0[2], q1[2];  // [slice] quant words for rows g, g+8
-            if (b & 1) {
-                // quants start 4-byte aligned (34 * odd + 2 = 0 mod 4)
-                q0[0] = *reinterpret_cast<const uint32_t *>(r0 + off + 2 + 4 * t);
-                q0[1] = *reinterpret_cast<const uint32_t *>(r0 + off + 18 + 4 * t);
-                q1[0] = *reinterpret_cast<const uint32_t *>(r1 + off + 2 + 4 * t);
-                q1[1] = *reinterpret_cast<const uint32_t *>(r1 + off + 18 + 4 * t);
-            } else {
-                const uint32_t *p0 = reinterpret_cast<const uint32_t *>(r0 + off + 4 * t);
-                const uint32_t *p1 = reinterpret_cast<const uint32_t *>(r1 + off + 4 * t);
-                q0[0] = __byte_perm(p0[0], p0[1], 0x5432);
-                q0[1] = __byte_perm(p0[4], p0[5], 0x5432);
-                q1[0] = __byte_perm(p1[0], p1[1], 0x5432);
-                q1[1] = __byte_perm(p1[4], p1[5], 0x5432);
+        if (nblk == 8) {
+            // full chunk: fetch the 16 B fragments first so their latency overlaps
+            uint2 xv[16];
+#pragma unroll
+            for (int s = 0; s < 16; ++s) {
+                xv[s] = xl[s * xstep];
+                if (!has_x) xv[s] = make_uint2(0u, 0u);
             }
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                __half2 lo0, hi0, lo1, hi1;
-                i8x4_to_h2x2(q0[h], lo0, hi0);
-                i8x4_to_h2x2(q1[h], lo1, hi1);
-                const uint32_t a0 = h2_as_u32(__hmul2(lo0, s0)), a2 = h2_as_u32(__hmul2(hi0, s0));
-                const uint32_t a1 = h2_as_u32(__hmul2(lo1, s1)), a3 = h2_as_u32(__hmul2(hi1, s1));
-                uint32_t b0 = 0, b1 = 0;
-                if (g < M) {
-                    const uint2 xv = sm.xs[((s_base + 2 * b + h) * M + g) * 4 + t];
-                    b0 = xv.x;
-                    b1 = xv.y;
-                }
-                mma_f16(c, a0, a1, a2, a3, b0, b1);
+            for (int b = 0; b < 8; ++b) q8_block(r0, r1, b * 34, (b & 1) != 0, t, xv[2 * b], xv[2 * b + 1], c);
+        } else {
+            for (int b = 0; b < nblk; ++b) {
+                uint2 x0 = xl[(2 * b) * xstep], x1 = xl[(2 * b + 1) * xstep];
+                if (!has_x) x0 = x1 = make_uint2(0u, 0u);
+                q8_block(r0, r1, b * 34, (b & 1) != 0, t, x0, x1, c);
             }
         }
     } else {
         const int ns = (elems + 15) / 16;
-#pragma unroll 4
-        for (int s = 0; s < ns; ++s) {
-            const uint2 w0 = *reinterpret_cast<const uint2 *>(r0 + s * 32 + 8 * t);
-            const uint2 w1 = *reinterpret_cast<const uint2 *>(r1 + s * 32 + 8 * t);
-            uint32_t b0 = 0, b1 = 0;
-            if (g < M) {
-                const uint2 xv = sm.xs[((s_base + s) * M + g) * 4 + t];
-                b0 = xv.x;
-                b1 = xv.y;
+        // slices in pairs (a register array indexed by a runtime value would live in local memory)
+#pragma unroll 2
+        for (int s = 0; s < ns; s += 2) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (s + h < ns) {
+                    const int sl = s + h;
+                    const uint2 w0 = *reinterpret_cast<const uint2 *>(r0 + sl * 32 + 8 * t);
+                    const uint2 w1 = *reinterpret_cast<const uint2 *>(r1 + sl * 32 + 8 * t);
+                    uint2 xv = xl[sl * xstep];
+                    if (!has_x) xv = make_uint2(0u, 0u);
+                    if constexpr (WT == kBF16)
+                        mma_bf16(c[h], w0.x, w1.x, w0.y, w1.y, xv.x, xv.y);
+                    else
+                        mma_f16(c[h], w0.x, w1.x, w0.y, w1.y, xv.x, xv.y);
+                }
             }
-            if constexpr (WT == kBF16)
-                mma_bf16(c, w0.x, w1.x, w0.y, w1.y, b0, b1);
-            else
-                mma_f16(c, w0.x, w1.x, w0.y, w1.y, b0, b1);
         }
     }
 }
@@ -181,43 +235,40 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     return (uint32_t)*reinterpret_cast<uint16_t *>(&ha) | ((uint32_t)*reinterpret_cast<uint16_t *>(&hb) << 16);
 }
 
-// Stage X (optionally RMS-normalised, rounded to T as the reference stores its
-// rmsnorm output) into the permuted fragment layout.
+// RMSNorm prologue: normalise X, rounded to T as the reference stores its
+// rmsnorm output (cuda.cu:533-601), into shared memory [M][Kpad] (zero padded).
 template <typename T>
-__device__ void stage_x(const GemvArgs &a, const Smem &sm, int Kpad) {
+__device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad) {
     const int M = a.M;
     const T *x = reinterpret_cast<const T *>(a.x);
-    if (a.norm_w) {
-        // one warp per activation row: sum of squares
-        const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        for (int m = wid; m < M; m += kWarps) {
-            const T *xr = x + (long)m * a.ldx;
-            float ss = 0.f;
-            for (int k = lane; k < a.K; k += 32) {
-                float v = to_float(xr[k]);
-                ss += v * v;
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) sm.misc[m] = rsqrtf(ss / (float)a.K + a.eps);
+    // one warp per activation row: sum of squares
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int m = wid; a.norm_w && m < M; m += kWarps) {
+        const T *xr = x + (long)m * a.ldx;
+        float ss = 0.f;
+        for (int k = lane; k < a.K; k += 32) {
+            float v = to_float(xr[k]);
+            ss += v * v;
         }
-        __syncthreads();
+        ss = warp_sum(ss);
+        if (lane == 0) sm.misc[m] = rsqrtf(ss / (float)a.K + a.eps);
     }
+    __syncthreads();
     const int nq = Kpad / 4;
     for (int i = threadIdx.x; i < nq * M; i += blockDim.x) {
-        const int m = i % M, kq = i / M;
+        const int m = i / nq, kq = i - m * nq;
         const int k = kq * 4;
         const T *xr = x + (long)m * a.ldx;
         float v[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float xv = (k + j < a.K) ? to_float(xr[k + j]) : 0.f;
-            if (a.norm_w && k + j < a.K) xv = (xv * sm.misc[m]) * a.norm_w[k + j];
-            v[j] = xv;
-        }
+        for (int j = 0; j < 4; ++j)
+            v[j] = (k + j < a.K) ? (a.norm_w ? (to_float(xr[k + j]) * sm.misc[m]) * a.norm_w[k + j]
+                                             : to_float(xr[k + j]))
+                                 : 0.f;
         uint2 pk;
         pk.x = pack2<T>(v[0], v[1]);
         pk.y = pack2<T>(v[2], v[3]);
-        sm.xs[((kq >> 2) * M + m) * 4 + (kq & 3)] = pk;
+        sm.xn[(long)m * nq + kq] = pk;
     }
 }
 
@@ -228,18 +279,20 @@ __device__ __forceinline__ uint64_t logits_key(long idx, int pack) {
     return ((uint64_t)bw << 58) | ((uint64_t)bl << 53) | ((uint64_t)j << 8) | e;
 }
 
+// Threads 0..127 own one (row r, column m) output of the 16 x 8 tile.
 template <typename T>
-__device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float (&best_v)[8], uint64_t (&best_k)[8]) {
-    // sum the warps' partial tiles: tid -> (row r, column m)
+__device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float &best_v, uint64_t &best_k) {
     const int tid = threadIdx.x;
-    const int r = tid >> 3, m = tid & 7;
+    const int r = (tid >> 3) & 15, m = tid & 7;
     float acc = 0.f;
+    if (tid < 128) {
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) acc += sm.red[(w * 16 + r) * 8 + m];
+        for (int w = 0; w < kWarps; ++w) acc += sm.red[(w * 16 + r) * 8 + m];
+    }
     __syncthreads();
-    sm.red[r * 8 + m] = acc;  // reduced tile in slot of warp 0
+    if (tid < 128) sm.red[r * 8 + m] = acc;  // reduced tile in the slot of warp 0
     __syncthreads();
-    if (m >= a.M || !row_valid(a, tile, r)) return;
+    if (tid >= 128 || m >= a.M || !row_valid(a, tile, r)) return;
     const int n = tile_row(a, tile, r);
     switch (a.epi) {
     case EPI_STORE: {
@@ -291,11 +344,11 @@ __device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float (&be
         const float y = round_to<T>(acc);
         if (a.out) reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(y);
         const long lim = (long)(a.N / a.pack) * a.pack;
-        if (n < lim && (y > best_v[m] || (y == best_v[m] && best_k[m] != ~0ull))) {
+        if (n < lim && (y > best_v || (y == best_v && best_k != ~0ull))) {
             const uint64_t k = logits_key(n, a.pack);
-            if (y > best_v[m] || k < best_k[m]) {
-                best_v[m] = y;
-                best_k[m] = k;
+            if (y > best_v || k < best_k) {
+                best_v = y;
+                best_k = k;
             }
         }
         break;
@@ -304,89 +357,77 @@ __device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float (&be
 }
 
 template <typename T, int WT>
-__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
     using F = WFmt<WT>;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int nchunks = (a.K + F::kChunk - 1) / F::kChunk;
     const int Kpad = nchunks * F::kChunk;
     Smem sm;
     sm.ring = smem_raw;
-    sm.bars = reinterpret_cast<uint64_t *>(sm.ring + (size_t)kWarps * kStages * kTileRows * kRowBytesMax);
-    sm.xs = reinterpret_cast<uint2 *>(sm.bars + kWarps * kStages);
-    sm.red = reinterpret_cast<float *>(sm.xs + (size_t)(Kpad / 4) * a.M);
+    sm.bars = reinterpret_cast<uint64_t *>(sm.ring + (size_t)kWarps * kStages * kStageBytes);
+    sm.xn = reinterpret_cast<uint2 *>(sm.bars + kWarps * kStages);
+    // X goes to shared memory when normalised here, or when small enough
+    const bool stage = a.norm_w || (size_t)a.M * Kpad * 2 <= kXStageMax;
+    sm.red = reinterpret_cast<float *>(sm.xn + (stage ? (size_t)(Kpad / 4) * a.M : 0));
     sm.misc = sm.red + kWarps * 16 * 8;
+    if (stage) {
+        sm.xsrc = sm.xn;
+        sm.xld = Kpad / 4;
+    } else {
+        sm.xsrc = reinterpret_cast<const uint2 *>(a.x);
+        sm.xld = a.ldx / 4;
+    }
 
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = num_tiles(a);
-    const bool bulk = a.bulk != 0;
+    const bool tma = a.bulk != 0;
     if (threadIdx.x < kWarps * kStages) mbar_init(sm.bars + threadIdx.x, 1);
     mbar_fence_init();
     __syncthreads();
+    if (threadIdx.x == 32 && a.pf) l2_prefetch_slice(a.pf, a.pf_bytes, blockIdx.x, gridDim.x);
 
-    // this warp's unit sequence: tiles blockIdx.x, +gridDim.x, ...; chunks w, w+4, ...
+    // this warp's unit sequence: tiles blockIdx.x, +gridDim.x, ...; chunks w, w+8, ...
     int p_tile = blockIdx.x, p_chunk = w;  // producer cursor
-    auto advance = [&](int &tile, int &chunk) {
-        chunk += kWarps;
-        if (chunk >= nchunks) {
-            chunk = w;
-            tile += gridDim.x;
-        }
-    };
-    // a warp with no chunk in this K (w >= nchunks) idles in the k-loop
-    const bool has_work = w < nchunks;
-    int issued = 0;
-    if (bulk && has_work) {
-        for (; issued < kStages && p_tile < ntiles; ++issued) {
-            issue_unit<WT>(a, sm, w, issued % kStages, p_tile, p_chunk, lane, true);
-            advance(p_tile, p_chunk);
-        }
-    }
-    // weights are ready to stream; wait for the producer of X, then let the next
-    // kernel in the stream start its own weight prefetch
+    const bool has_work = w < nchunks;     // a warp with no chunk in this K idles in the k-loop
+    if (tma)
+        for (int s = 0; s < kStages; ++s) produce_unit<WT>(a, sm, w, s, lane, has_work, ntiles, nchunks, p_tile, p_chunk);
+    // weights are in flight; wait for the producer of X, then let the next kernel
+    // in the stream start its own weight prefetch
     pdl_wait();
     pdl_trigger();
-    stage_x<T>(a, sm, Kpad);
+    if (stage) stage_xn<T>(a, sm, Kpad);
     __syncthreads();
 
-    float best_v[8];
-    uint64_t best_k[8];
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-        best_v[m] = -INFINITY;
-        best_k[m] = ~0ull;
-    }
-
+    float best_v = -INFINITY;
+    uint64_t best_k = ~0ull;
     int consumed = 0;
+    bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         if (has_work) {
             for (int chunk = w; chunk < nchunks; chunk += kWarps) {
                 const int slot = consumed % kStages;
-                bool ready = true;
-                if (bulk) {
-                    // a copy that never lands is reported, not waited on forever
-                    ready = mbar_wait_bounded(sm.bars + w * kStages + slot, (consumed / kStages) & 1, a.err, 1);
+                if (tma) {
+                    // a box that never lands is reported (bounded wait), not waited on forever
+                    if (!mbar_wait_bounded(sm.bars + w * kStages + slot, (consumed / kStages) & 1, a.err, 1))
+                        ok = false;
                 } else {
                     issue_unit<WT>(a, sm, w, slot, tile, chunk, lane, false);
+                    __syncwarp();
                 }
-                if (ready) consume_unit<WT>(a, sm, w, slot, chunk, lane, c);
-                __syncwarp();
+                if (ok) consume_unit<WT>(a, sm, w, slot, chunk, lane, c);
+                __syncwarp();  // the slot is free again
                 ++consumed;
-                if (bulk && p_tile < ntiles) {
-                    // refill the slot just consumed
-                    issue_unit<WT>(a, sm, w, (issued) % kStages, p_tile, p_chunk, lane, true);
-                    ++issued;
-                    advance(p_tile, p_chunk);
-                }
+                if (tma && ok) produce_unit<WT>(a, sm, w, slot, lane, has_work, ntiles, nchunks, p_tile, p_chunk);
             }
         }
         // partial tile of this warp -> shared memory (rows g, g+8; columns 2t, 2t+1)
         const int g = lane >> 2, t = lane & 3;
         float *red = sm.red + w * 16 * 8;
-        red[g * 8 + 2 * t] = c[0];
-        red[g * 8 + 2 * t + 1] = c[1];
-        red[(g + 8) * 8 + 2 * t] = c[2];
-        red[(g + 8) * 8 + 2 * t + 1] = c[3];
+        red[g * 8 + 2 * t] = c[0][0] + c[1][0];
+        red[g * 8 + 2 * t + 1] = c[0][1] + c[1][1];
+        red[(g + 8) * 8 + 2 * t] = c[0][2] + c[1][2];
+        red[(g + 8) * 8 + 2 * t + 1] = c[0][3] + c[1][3];
         __syncthreads();
         epilogue<T>(a, sm, tile, best_v, best_k);
         __syncthreads();
@@ -395,14 +436,16 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
     if (a.epi == EPI_LOGITS) {
         // per-CTA argmax partials: reduce over the 16 row-threads of each column m
         const int tid = threadIdx.x, m = tid & 7;
-        float v = best_v[m];
-        uint64_t k = best_k[m];
-        float *sv = sm.misc;  // [16][8]
-        uint64_t *sk = reinterpret_cast<uint64_t *>(sm.misc + 128);
-        sv[tid] = v;
-        sk[tid] = k;
+        float *sv = sm.misc + 8;                                        // [16][8]
+        uint64_t *sk = reinterpret_cast<uint64_t *>(sm.misc + 8 + 128);  // [16][8]
+        if (tid < 128) {
+            sv[tid] = best_v;
+            sk[tid] = best_k;
+        }
         __syncthreads();
         if (tid < 8 && tid < a.M) {
+            float v = sv[tid];
+            uint64_t k = sk[tid];
             for (int r = 1; r < 16; ++r) {
                 const float ov = sv[r * 8 + tid];
                 const uint64_t ok = sk[r * 8 + tid];
@@ -414,6 +457,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
             a.part_val[(long)blockIdx.x * 8 + tid] = v;
             a.part_key[(long)blockIdx.x * 8 + tid] = k;
         }
+        (void)m;
         // the last CTA to finish reduces the partials to token ids
         __shared__ int last;
         __threadfence();
@@ -447,18 +491,23 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const GemvArgs a) {
     }
 }
 
-size_t gemv_smem_bytes(int K, int M, int wt) {
+size_t gemv_smem_bytes(int K, int M, int wt, bool norm) {
     const int chunk = wt == kQ8_0 ? WFmt<kQ8_0>::kChunk : WFmt<kF16>::kChunk;
     const int Kpad = (K + chunk - 1) / chunk * chunk;
-    return (size_t)kWarps * kStages * kTileRows * kRowBytesMax + kWarps * kStages * 8 + (size_t)(Kpad / 4) * M * 8 +
-           kWarps * 16 * 8 * 4 + 128 * 4 + 128 * 8;
+    const bool stage = norm || (size_t)M * Kpad * 2 <= kXStageMax;
+    return (size_t)kWarps * kStages * kStageBytes + kWarps * kStages * 8 + (stage ? (size_t)Kpad * M * 2 : 0) +
+           kWarps * 16 * 8 * 4 +
+           (8 + 128) * 4 + 128 * 8;
 }
 
 template <typename T, int WT> void launch(const GemvArgs &a, int grid, size_t smem, cudaStream_t s, bool pdl) {
     auto kern = gemv_kernel<T, WT>;
-    static bool configured[2] = {false, false};
-    (void)configured;
-    WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // raise the dynamic shared-memory limit only when a launch needs more
+    static int configured = 0;
+    if ((int)smem > configured) {
+        WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = (int)smem;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kWarps * 32);
@@ -484,15 +533,41 @@ bool gemv_supported(int wtype, int act, int K) {
 void gemv(GemvArgs a, int act, cudaStream_t s) {
     if (a.M <= 0 || a.M > 8) WK_PANIC("gemv: M=%d outside [1, 8]", a.M);
     if (!gemv_supported(a.wtype, act, a.K)) WK_PANIC("gemv: unsupported wtype %d / act %d / K %d", a.wtype, act, a.K);
-    const int chunkb = a.wtype == kQ8_0 ? 272 : 256;
     const long rb = a.wtype == kQ8_0 ? (long)(a.K / 32) * 34 : (long)a.K * 2;
-    (void)chunkb;
-    a.bulk = ((uintptr_t)a.w % 16 == 0) && (rb % 16 == 0) ? 1 : 0;
+    // weight tiles stream by TMA when rows are 16-byte aligned
+    const CUtensorMap *map = nullptr;
+    if (((uintptr_t)a.w % 16 == 0) && (rb % 16 == 0)) {
+        const int box_inner = a.wtype == kQ8_0 ? WFmt<kQ8_0>::kRowB / 2 : WFmt<kF16>::kRowB / 2;
+        const long rows = a.epi == EPI_SWIGLU ? 2L * a.F : (long)a.N;
+        map = weight_map(a.w, rows, rb, box_inner, a.epi == EPI_SWIGLU ? 8 : kTileRows);
+    }
+    a.bulk = map ? 1 : 0;
+    if (map) a.wmap = *map;
     if (!a.err) a.err = g_rt.d_error;
-    const size_t smem = gemv_smem_bytes(a.K, a.M, a.wtype);
-    if ((int)smem > g_rt.max_smem_optin) WK_PANIC("gemv: K=%d M=%d needs %zu B of shared memory", a.K, a.M, smem);
+    if (((uintptr_t)a.x % 8) || (a.ldx % 4)) WK_PANIC("gemv: activations must be 8-byte aligned rows");
+    const size_t smem = gemv_smem_bytes(a.K, a.M, a.wtype, a.norm_w != nullptr);
+    if ((int)smem > g_rt.max_smem_optin) {
+        // the normalised X does not fit beside the ring: split the activation rows
+        if (a.M == 1) WK_PANIC("gemv: K=%d needs %zu B of shared memory", a.K, smem);
+        const int m1 = a.M / 2;
+        const size_t es = act == kF32 ? 4 : 2;
+        GemvArgs b = a;
+        b.M = a.M - m1;
+        a.M = m1;
+        b.x = (const char *)a.x + (size_t)m1 * a.ldx * es;
+        if (b.epi != EPI_LOGITS) b.out = (char *)a.out + (size_t)m1 * a.ldo * es;
+        if (b.res) b.res = (const char *)a.res + (size_t)m1 * a.ldr * es;
+        if (b.pos) b.pos += m1;
+        if (b.seq) b.seq += m1;
+        if (b.tokens) b.tokens += m1;
+        if (b.epi == EPI_LOGITS && b.out) b.out = (char *)a.out + (size_t)m1 * a.ldo * es;
+        gemv(a, act, s);
+        gemv(b, act, s);
+        return;
+    }
     const int ntiles = a.epi == EPI_SWIGLU ? (a.F + 7) / 8 : (a.N + kTileRows - 1) / kTileRows;
-    int per_sm = smem <= 100 * 1024 ? 2 : 1;
+    // two CTAs per SM when both fit (about 200 KB of weight tiles in flight per SM)
+    const int per_sm = 2 * (smem + 1024) <= (size_t)g_rt.smem_per_sm ? 2 : 1;
     int grid = ntiles < g_rt.num_sms * per_sm ? ntiles : g_rt.num_sms * per_sm;
     if (a.epi == EPI_LOGITS && grid > kMaxLogitCtas) grid = kMaxLogitCtas;
     const bool pdl = g_rt.pdl && a.pdl;

@@ -113,6 +113,25 @@ void fill_block_table(int *bt, int batch, int pages, cudaStream_t s) {
 void matmul(void *out, const void *x, const void *w, const void *bias, int M, int K, int N, int wtype, int act,
             cudaStream_t s) {
     if (M <= 0 || N <= 0) return;
+    const size_t es0 = act_size(act);
+    if (M >= kTcMinRows && g_rt.tc_gemm && gemm_tc_supported(wtype, act, K, N, EPI_STORE, 0) &&
+        ((uintptr_t)x % 16) == 0 && ((uintptr_t)w % 16) == 0 && ((size_t)K * es0) % 16 == 0 &&
+        (wtype != kQ8_0 || ((size_t)(K / 32) * 34) % 16 == 0)) {
+        GemmArgs a;
+        a.w = (const uint8_t *)w;
+        a.wtype = wtype;
+        a.N = N;
+        a.K = K;
+        a.x = x;
+        a.ldx = K;
+        a.M = M;
+        a.epi = EPI_STORE;
+        a.out = out;
+        a.ldo = N;
+        a.bias = bias;
+        gemm_tc(a, act, s);
+        return;
+    }
     if (gemv_supported(wtype, act, K)) {
         const size_t es = act_size(act);
         for (int m0 = 0; m0 < M; m0 += 8) {

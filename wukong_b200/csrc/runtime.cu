@@ -79,6 +79,7 @@ void cuda_init(int idx) {
     WK_CHECK(cudaGetDeviceProperties(&prop, idx));
     g_rt.num_sms = prop.multiProcessorCount;
     g_rt.max_smem_optin = (int)prop.sharedMemPerBlockOptin;
+    g_rt.smem_per_sm = (int)prop.sharedMemPerMultiprocessor;
     if (prop.major < 10) WK_PANIC("this library is built for sm_100a (B200); device %d is sm_%d%d", idx, prop.major, prop.minor);
     // error word in mapped pinned memory: kernels write it, the host reads it
     // after any synchronisation without an extra copy
@@ -87,6 +88,8 @@ void cuda_init(int idx) {
     WK_CHECK(cudaHostGetDevicePointer((void **)&g_rt.d_error, g_rt.h_error, 0));
     const char *pdl = getenv("WUKONG_PDL");
     g_rt.pdl = !(pdl && pdl[0] == '0');
+    const char *tc = getenv("WUKONG_TC_GEMM");
+    g_rt.tc_gemm = !(tc && tc[0] == '0');
     printf("Running on GPU %d: %s, Compute Capability %d.%d\n", idx, prop.name, prop.major, prop.minor);
     fflush(stdout);
     layers_init();
@@ -122,6 +125,7 @@ void cuda_free(void *ptr) {
     if (!ptr) return;
     ensure_init();
     prefix_cache_forget(ptr);
+    forget_weight_maps(ptr);
     WK_CHECK(cudaFreeAsync(ptr, g_rt.stream));
 }
 

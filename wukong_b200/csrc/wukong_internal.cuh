@@ -1,14 +1,27 @@
 // Declarations shared between the library's translation units.
 #pragma once
+#include <cuda.h>  // CUtensorMap (types only; the encoder is fetched at run time)
+
 #include "common.cuh"
 
 namespace wk {
+
+// ---------------------------------------------------------------- TMA (tma.cu)
+// Tensor maps are encoded on the host with cuTensorMapEncodeTiled, resolved via
+// cudaGetDriverEntryPoint so that the library links without libcuda.
+bool encode_map_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+// Cached map over a weight matrix viewed as [N rows][row_bytes / 2] uint16 with
+// boxes of `box_inner` uint16 x `box_rows` rows (null if the rows are not TMA-able).
+const CUtensorMap *weight_map(const void *w, long rows, long row_bytes, int box_inner, int box_rows);
+void forget_weight_maps(const void *w);
 
 // ---------------------------------------------------------------- GEMV (gemv.cu)
 enum Epi : int { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
 constexpr int kMaxLogitCtas = 512;
 
 struct GemvArgs {
+    CUtensorMap wmap;  // weight tiles (64-byte aligned first member; set by gemv())
     const uint8_t *w = nullptr;  // weight rows, raw GGUF bytes [N, K]
     int wtype = kQ8_0;
     int N = 0, K = 0;
@@ -39,13 +52,49 @@ struct GemvArgs {
     int *counter = nullptr;
     int *tokens = nullptr;
     int pack = 8;
+    const void *pf = nullptr;  // weights of a later kernel to prefetch into L2
+    long pf_bytes = 0;
     int *err = nullptr;
-    int bulk = 1;  // set by gemv()
+    int bulk = 1;  // set by gemv(): 1 when the weight tiles stream by TMA
     int pdl = 1;   // launch with programmatic dependent launch
 };
+static_assert(alignof(GemvArgs) >= 64, "the tensor map must stay 64-byte aligned");
 
 bool gemv_supported(int wtype, int act, int K);
 void gemv(GemvArgs a, int act, cudaStream_t s);
+
+// ---------------------------------------------------------------- tcgen05 GEMM (gemm_tc.cu)
+// Same epilogues as the GEMV (no LOGITS), any M, 16-byte aligned rows.
+struct GemmArgs {
+    CUtensorMap wmap;  // weights (set by gemm_tc)
+    CUtensorMap xmap;  // activations (set by gemm_tc)
+    const uint8_t *w = nullptr;
+    int wtype = kQ8_0;
+    int N = 0, K = 0;
+    const void *x = nullptr;
+    long ldx = 0;
+    int M = 0;
+    int epi = EPI_STORE;
+    void *out = nullptr;
+    long ldo = 0;
+    const void *bias = nullptr;
+    const void *res = nullptr;
+    long ldr = 0;
+    int nq = 0, nk = 0, hd = 0;
+    const float *freqs = nullptr;
+    const int *pos = nullptr;
+    const int *seq = nullptr;
+    void *kpool = nullptr, *vpool = nullptr;
+    const int *block_table = nullptr;
+    int max_pages = 0, page = 0, kv_heads = 0;
+    int F = 0;
+    int *err = nullptr;
+    int pdl = 1;
+};
+bool gemm_tc_supported(int wtype, int act, int K, int N, int epi, int F);
+void gemm_tc(GemmArgs a, int act, cudaStream_t s);
+// Minimum activation rows for which the tcgen05 GEMM replaces the GEMV.
+constexpr int kTcMinRows = 16;
 
 // ---------------------------------------------------------------- ops.cu
 template <typename T> void dequant_q8_0(T *out, const void *in, long nblocks, cudaStream_t s);
@@ -67,7 +116,8 @@ struct PagedKV {
 };
 template <typename T>
 void attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
-                     int nrows, int max_len, const PagedKV &c, int H, cudaStream_t s, bool pdl);
+                     int nrows, int max_len, const PagedKV &c, int H, cudaStream_t s, bool pdl,
+                     const void *pf = nullptr, long pf_bytes = 0);
 template <typename T>
 void attention_qkv_rows(T *out, const T *qkv, int B, int Tn, int NH, int kvNH, int HS, cudaStream_t s);
 
