@@ -75,6 +75,22 @@ int wk_gemv(void *out, const void *x, const void *w, int M, int K, int N, int wt
 /* library stream (cudaStream_t) so hosts can order their own work */
 void *wk_stream(void);
 
+/* No counterpart in the reference.  cuda_predict without device allocation,
+ * for hosts that cannot call cudaMalloc at that point: a process that has
+ * given all free HBM to its own KV-cache pool, or a latency-critical loop in
+ * which cudaMalloc / cudaFree would synchronise the device.  Same arguments
+ * and result as cuda_predict (greedy next-token ids, int32 [batch], of the
+ * last row of each of the batch sequences in ff) for F16, BF16 and Q8_0
+ * output weights, same kernel.  Its scratch is a fixed 393,472-byte array
+ * inside the library (every GPU that loads the library holds it until exit),
+ * so a call takes at most 64 sequences and col <= 32768; larger or unsupported
+ * sizes return -1 with the reason in wk_last_error().  All calls share that
+ * array: calls that overlap on the GPU race; calls on the library stream do
+ * not.  The first call on a device looks up the array's address; make it
+ * before any stream capture.  Returns 0 on success. */
+int wk_predict_noalloc(int *out, const void *ff, const void *norm_weight, const void *out_weight, int batch,
+                       int row, int col, int wsize, float eps, int dtype);
+
 #ifdef __cplusplus
 }
 #endif

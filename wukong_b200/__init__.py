@@ -69,6 +69,7 @@ EXT = {
     "wk_fill_random_f16": (_I, [_P, _L, _U64, _F]),
     "wk_fill_const_f32": (_I, [_P, _L, _F]),
     "wk_gemv": (_I, [_P, _P, _P, _I, _I, _I, _I]),
+    "wk_predict_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _F, _I]),
 }
 
 

@@ -18,9 +18,7 @@
 
 namespace wk {
 
-namespace {
-
-char g_err[512] = "";
+static char g_err[512] = "";
 
 int fail(const char *fmt, ...) {
     va_list ap;
@@ -29,6 +27,8 @@ int fail(const char *fmt, ...) {
     va_end(ap);
     return -1;
 }
+
+namespace {
 
 #define WK_TRY(call)                                                                 \
     do {                                                                             \

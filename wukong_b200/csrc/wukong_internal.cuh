@@ -131,6 +131,10 @@ void fill_row_meta(int *seq, int *pos, int rows, int n, int pos0, cudaStream_t s
 // Identity block table: bt[b][p] = b * pages + p.
 void fill_block_table(int *bt, int batch, int pages, cudaStream_t s);
 
+// ---------------------------------------------------------------- engine.cu
+// Records the message returned by wk_last_error() and returns -1.
+int fail(const char *fmt, ...);
+
 // ---------------------------------------------------------------- layers.cu
 void layers_init();
 void layers_fini();
