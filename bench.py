@@ -1,30 +1,31 @@
-"""Benchmark: greedy decode tokens/s of Llama-3.2-1B with Q8_0 weights on B200.
+"""Benchmark: greedy decode tokens/s of Llama-3 with Q8_0 weights on B200.
 
-Workload (default): Llama-3.2-1B architecture (16 layers, d 2048, 32/8 heads,
-head_dim 64, SwiGLU 8192, vocab 128256, RoPE theta 500000, RMSNorm eps 1e-5),
-random-init weights: linear layers and output.weight Q8_0 (w ~ N(0, 0.02)
-quantised GGUF-style), token_embd F16, norms 1.0; batch 1 (--batch), a
-128-token uniform-random prompt, then greedy decode.  A step is one decode step
-(one token per sequence).  Weights per step (1.31 GB) exceed the 126 MB L2, so
-no flush is needed between steps.
+Workload (default, --model 1b): Llama-3.2-1B architecture (16 layers, d 2048,
+32/8 heads, head_dim 64, SwiGLU 8192, vocab 128256, RoPE theta 500000, RMSNorm
+eps 1e-5), random-init weights generated on the device: linear layers and
+output.weight Q8_0 (w ~ N(0, 0.02) quantised GGUF-style), token_embd F16,
+norms 1.0; batch 1 (--batch), a 128-token uniform-random prompt, then greedy
+decode.  A step is one decode step (one token per sequence).  The weights read
+per step (1.31 GB) exceed the 126 MB L2, so no flush is needed between steps.
+--model 8b / 70b: Llama-3.1-8B / -70B shapes with a 2048 / 4096-token prompt.
 
 Arms
-  (default)            the native engine (wukong_ext.h): CUDA-graph decode step,
-                       inputs resident in HBM -> `value`; `e2e` runs the
-                       reference's Go call sequence (llama.go Predict per step)
-                       through the cuda.h ABI with host buffers and the prefix
-                       cache on.
-  --impl reference     the reference's CPU path: the reference has none (its
-                       only Runner is CUDA, llm/array.go:123-135), so this times
-                       the C++ CPU restatement of its semantics (oracle/) on all
-                       host cores.
-  --impl reference-gpu (extra) the reference's own cuda.cu built for sm_100a,
-                       driven by the same Go-loop host mirror (full re-prefill
-                       per step, as llm/model.go does).
+  (default)          the native engine (wukong_ext.h): CUDA-graph decode step,
+                     inputs resident in HBM -> `value`.  `e2e`: for 1b, the
+                     reference's Go call sequence (llama.go Predict per step)
+                     through the cuda.h ABI with host ids in and the host token
+                     out, prefix cache on; for tensor-parallel runs, the engine
+                     with the step's ids copied from pinned host memory and the
+                     tokens read back every step.
+  --impl reference   the reference's CPU path: the reference has none (its only
+                     Runner is CUDA, llm/array.go:123-135), so this times the C++
+                     CPU restatement of its semantics (oracle/) on all host cores.
+  --op NxKxM,...     the single Q8_0 dequant-matmul op through cuda_matmul.
 
-Multi-GPU: the 1B decode does not shard; --gpus N runs N independent replicas
-(one process per GPU under torchrun), value = tokens/s summed over ranks with
-the max time over ranks.
+Multi-GPU: 1b does not shard (replicas: --gpus N runs N independent copies,
+one process per GPU, value = tokens/s summed over ranks, weak scaling); 8b and
+70b are tensor-parallel over the N GPUs (one model, value = its tokens/s,
+strong scaling).  Times are the max over ranks of CUDA-event durations.
 """
 import argparse
 import ctypes
@@ -45,8 +46,9 @@ sys.path.insert(0, ROOT)
 os.environ.setdefault("WUKONG_PREFIX_CACHE", "1")
 
 METRIC = "decode tokens/sec (batch 1, Q8_0)"
-CFG_1B = dict(L=16, d=2048, H=32, Hk=8, D=64, F=8192, V=128256, eps=1e-5, theta=500000.0)
-PROMPT = 128
+PROMPTS = {"1b": 128, "8b": 2048, "70b": 4096}
+NAMES = {"1b": "Llama-3.2-1B", "8b": "Llama-3.1-8B", "70b": "Llama-3.1-70B"}
+SEED = 1234
 
 
 def peaks():
@@ -58,14 +60,16 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def step_bytes(cfg, ctx_avg, batch):
-    """Algorithmic HBM bytes of one decode step: every weight once (Q8_0 =
-    34/32 bytes per element) plus the K/V rows read by attention."""
-    d, H, Hk, D, F, V, L = cfg["d"], cfg["H"], cfg["Hk"], cfg["D"], cfg["F"], cfg["V"], cfg["L"]
-    per_layer = ((H + 2 * Hk) * D * d + d * d + 2 * F * d + d * F) * 34 // 32
-    logits = V * d * 34 // 32
-    kv = batch * ctx_avg * L * 2 * Hk * D * 2
-    return L * per_layer + logits + kv
+def profiled_traffic(name):
+    """DRAM bytes per launch of a kernel from its committed ncu summary
+    (a `traffic_bytes_per_launch: N` line in profiles/<name>.md), or None."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":", 1)[1].strip().split()[0])
+    return None
 
 
 class Clocks:
@@ -112,43 +116,50 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def make_model_host(cfg, seed):
-    from oracle import oracle as orc
-    from tests.model_util import make_weights
-    return make_weights(cfg, 8, 8, 1, seed=seed, ctx=PROMPT + 512 + 64)
+def kv_bytes(cfg, ctx_avg, batch, world):
+    """K/V rows read by attention per step on one rank (fp16)."""
+    return batch * ctx_avg * cfg["L"] * 2 * (cfg["Hk"] // world) * cfg["D"] * 2
 
 
 # ------------------------------------------------------------------ our arm
-def run_ours(args, rank, world):
+def run_ours(args, rank, world, local_rank):
     import torch
     import wukong_b200 as wk
-    from tests.model_util import DeviceModel, build_engine, host_mirror
+    from wukong_b200.engine import LLAMA, Engine, HostLlama, SyntheticLlama
 
-    torch.cuda.set_device(rank % max(1, torch.cuda.device_count()))
+    torch.cuda.set_device(local_rank)
     L = wk.lib()
-    L.cuda_init(rank % max(1, torch.cuda.device_count()))
-    cfg = dict(CFG_1B)
-    B, K, W = args.batch, args.steps, args.warmup
-    ctx = PROMPT + W + K + 8
-    w = make_model_host(cfg, seed=1234)
-    dm = DeviceModel(w)
-    m = build_engine(dm, w, cfg, 8, 8, 1, max_batch=B, ctx=ctx)
-    prompt = np.random.default_rng(7).integers(0, cfg["V"], size=(B, PROMPT)).astype(np.int32)
+    L.cuda_init(local_rank)
+    cfg = dict(LLAMA[args.model])
+    tpw = world if args.model != "1b" else 1
+    if tpw > 1:
+        idbuf = ctypes.create_string_buffer(128)
+        if rank == 0:
+            wk.check(L.wk_tp_unique_id(idbuf))
+        t = torch.frombuffer(bytearray(idbuf.raw), dtype=torch.uint8).cuda()
+        torch.distributed.broadcast(t, 0)
+        wk.check(L.wk_tp_init(rank, world, bytes(t.cpu().numpy())))
+    B, K, W, P = args.batch, args.steps, args.warmup, args.prompt
+    ctx = P + W + K + 8
+    e2e_abi = not args.no_e2e and tpw == 1
+    sm = SyntheticLlama(cfg, ctx, seed=SEED, unfused=e2e_abi, tp_rank=rank if tpw > 1 else 0, tp_world=tpw)
+    eng = Engine.from_synthetic(sm, max_batch=B, tp=tpw > 1)
+    prompt = np.random.default_rng(7).integers(0, cfg["V"], size=(B, P)).astype(np.int32)
     d_prompt = L.cuda_malloc(prompt.nbytes)
     L.cuda_to_device(d_prompt, prompt.ctypes.data_as(ctypes.c_void_p), prompt.nbytes)
-    wk.check(L.wk_model_prefill(m, d_prompt, B, PROMPT, None))
+    eng.prefill(d_prompt, B, P)
     stream = torch.cuda.ExternalStream(L.wk_stream())
     for _ in range(W):
-        wk.check(L.wk_model_decode_step(m))
+        eng.step()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(rank) as clk:
+    with Clocks(local_rank) as clk:
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(K):
-            L.wk_model_decode_step(m)
+            L.wk_model_decode_step(eng.m)
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
@@ -156,21 +167,25 @@ def run_ours(args, rank, world):
         t = torch.tensor([ms], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-    launches = L.wk_model_step_launches(m)
-    ctx_avg = PROMPT + W + K // 2
-    sb = step_bytes(cfg, ctx_avg, B)
-    res = dict(ms=ms, launches=launches, clocks=clk.summary(), step_bytes=sb)
+    res = dict(ms=ms, launches=eng.launches_per_step(), clocks=clk.summary(), tp=tpw,
+               step_bytes=sm.weight_bytes_per_step() + kv_bytes(cfg, P + W + K // 2, B, tpw))
 
-    # dominant kernel: the Q8_0 dequant-GEMV at the FFN up|gate shape (16384 x 2048),
-    # timed alone over 8 rotating weight copies (> L2) with CUDA events
-    res["gemv"] = time_gemv(L, stream, N=16384, K=2048, M=B)
-    res["gemv_op"] = time_gemv(L, stream, N=8192, K=2048, M=B)
+    # dominant kernel: the Q8_0 dequant-GEMV at the FFN up|gate shape of the
+    # model (per rank), timed alone over 8 rotating weight copies (> L2)
+    if rank == 0:
+        res["gemv"] = time_gemv(L, stream, N=2 * sm.local["F"], K=cfg["d"], M=B)
+        res["gemv_op"] = time_gemv(L, stream, N=8192, K=2048, M=B)
 
-    # e2e: the Go call sequence through cuda.h (host ids in, host token out), prefix cache on
     if not args.no_e2e:
-        res["e2e"] = run_e2e(L, dm, cfg, B, K, W, prompt)
-    L.wk_model_destroy(m)
-    dm.free()
+        if e2e_abi:
+            res["e2e"] = run_e2e_abi(L, sm, B, K, W, prompt)
+        else:
+            res["e2e"] = run_e2e_engine(L, eng, B, K, W, world)
+    eng.destroy()
+    sm.free()
+    L.cuda_free(d_prompt)
+    if tpw > 1:
+        L.wk_tp_fini()
     return res
 
 
@@ -200,11 +215,12 @@ def time_gemv(L, stream, N, K, M, copies=8, reps=20):
     return dict(N=N, K=K, M=M, us=us, bytes=byts, gbs=byts / us / 1e3)
 
 
-def run_e2e(L, dm, cfg, B, K, W, prompt):
-    import torch
-    from tests.model_util import host_mirror
-    ctx = PROMPT + W + K + 8
-    h, _ = host_mirror(dm, cfg, 8, 8, 1, ctx)
+def run_e2e_abi(L, sm, B, K, W, prompt):
+    """The reference's Go call sequence through cuda.h (host ids in, host token
+    out every step), with the prefix cache on."""
+    from wukong_b200.engine import HostLlama
+    h = HostLlama(sm)
+    ctx = sm.ctx
     seqs = [list(prompt[b]) for b in range(B)]
     buf = np.zeros((B, ctx), np.int32)
     out = np.zeros(B, np.int32)
@@ -213,9 +229,7 @@ def run_e2e(L, dm, cfg, B, K, W, prompt):
         n = len(seqs[0])
         for b in range(B):
             buf[b, :n] = seqs[b]
-        ids = np.ascontiguousarray(buf[:, :n])
-        rc = L.wk_host_llama_predict(h, ids.ctypes.data_as(ctypes.c_void_p), B, n, out.ctypes.data_as(ctypes.c_void_p))
-        assert rc == 0
+        h.predict(buf[:, :n], out)
         for b in range(B):
             seqs[b].append(int(out[b]))
         return n
@@ -227,23 +241,98 @@ def run_e2e(L, dm, cfg, B, K, W, prompt):
     for _ in range(K):
         h2d += 4 * B * step()
     dt = time.perf_counter() - t0
-    L.wk_host_llama_destroy(h)
+    h.destroy()
     return dict(value=B * K / dt, unit="tokens/s", h2d_bytes_per_step=h2d // K, d2h_bytes_per_step=4 * B,
                 path="cuda.h ABI, llama.go call sequence, WUKONG_PREFIX_CACHE=1")
 
 
+def run_e2e_engine(L, eng, B, K, W, world):
+    """The engine with host I/O every step: the step's ids are copied from
+    pinned host memory, the step runs, its tokens are read back."""
+    import torch
+    ids = torch.zeros(B, dtype=torch.int32).pin_memory()
+    toks = torch.zeros(B, dtype=torch.int32).pin_memory()
+    nxt = L.wk_model_next_ids(eng.m)
+    cur = L.wk_model_tokens(eng.m)
+
+    def step():
+        L.cuda_to_device(nxt, ctypes.c_void_p(ids.data_ptr()), 4 * B)
+        L.wk_model_decode_step(eng.m)
+        L.cuda_to_host(ctypes.c_void_p(toks.data_ptr()), cur, 4 * B)
+        ids.copy_(toks)
+
+    L.cuda_to_host(ctypes.c_void_p(toks.data_ptr()), cur, 4 * B)
+    ids.copy_(toks)
+    for _ in range(W):
+        step()
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        step()
+    dt = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([dt], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dt = float(t.item())
+    return dict(value=B * K / dt, unit="tokens/s", h2d_bytes_per_step=4 * B, d2h_bytes_per_step=4 * B,
+                path="wukong_ext.h engine, ids from pinned host memory and tokens back every step")
+
+
+def run_op(spec, copies=8, reps=20):
+    """The single Q8_0 dequant-matmul op: W [N, K] Q8_0 (8 rotating copies, >
+    L2 for the default shapes), X [M, K] fp16, out [M, N] fp16, through
+    cuda_matmul (GEMV for M <= 8, tcgen05 GEMM for M >= 16)."""
+    import torch
+    import wukong_b200 as wk
+    L = wk.lib()
+    L.cuda_init(0)
+    stream = torch.cuda.ExternalStream(L.wk_stream())
+    hbm, src = peaks()
+    for item in spec.split(","):
+        N, K, M = (int(v) for v in item.lower().split("x"))
+        rb = N * (K // 32) * 34
+        ws = [L.cuda_malloc(rb) for _ in range(copies)]
+        for i, p in enumerate(ws):
+            L.wk_fill_random_q8_0(p, N, K, 77 + i, 0.02)
+        x = L.cuda_malloc(2 * M * K)
+        L.wk_fill_random_f16(x, M * K, 5, 1.0)
+        o = L.cuda_malloc(2 * M * N)
+        for i in range(3):
+            L.cuda_matmul(o, x, ws[i % copies], None, M, K, N, 8)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = reps * copies
+        e0.record(stream)
+        for i in range(n):
+            L.cuda_matmul(o, x, ws[i % copies], None, M, K, N, 8)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000 / n
+        byts = rb + 2 * M * K + 2 * M * N
+        print(json.dumps({"op": "cuda_matmul Q8_0", "N": N, "K": K, "M": M, "us": us, "bytes": byts,
+                          "gbs": byts / us / 1e3, "hbm_frac": byts / us / 1e3 / hbm, "peak_source": src,
+                          "tflops": 2.0 * M * N * K / us / 1e6}))
+        for p in ws + [x, o]:
+            L.cuda_free(p)
+    L.cuda_fini()
+
+
 # ------------------------------------------------------------------ CPU baseline
-def run_cpu(cfg, B, steps, budget_s=25.0):
+def run_cpu(model, B, P, steps, budget_s=25.0):
     """The oracle port (C++ restatement of the reference semantics) on the host
-    cores: prefill the 128-token prompt, then time greedy decode steps until the
-    step budget or the time budget is used."""
+    cores, on the same synthetic model (the oracle's generator is bit-identical
+    to the device one): prefill the prompt, then time greedy decode steps until
+    the step budget or the time budget is used."""
     from oracle import oracle as orc
-    from tests.model_util import oracle_model
+    from tests.model_util import make_weights, oracle_model
+    from wukong_b200.engine import LLAMA
+    cfg = dict(LLAMA[model])
     orc.set_threads(os.cpu_count() or 1)
-    w = make_model_host(cfg, seed=1234)
-    om = oracle_model(w, cfg, 8, 8, 1, PROMPT + steps + 16)
+    w = make_weights(cfg, 8, 8, 1, seed=SEED, ctx=P + steps + 16)
+    om = oracle_model(w, cfg, 8, 8, 1, P + steps + 16)
     om.reset(B)
-    prompt = np.random.default_rng(7).integers(0, cfg["V"], size=(B, PROMPT)).astype(np.int32)
+    prompt = np.random.default_rng(7).integers(0, cfg["V"], size=(B, P)).astype(np.int32)
     tok, _, _ = om.forward(prompt)
     t0 = time.perf_counter()
     n = 0
@@ -252,44 +341,7 @@ def run_cpu(cfg, B, steps, budget_s=25.0):
         n += 1
     dt = time.perf_counter() - t0
     return dict(value=B * n / dt, unit="tokens/s", cores=orc.num_threads(), kind="port",
-                sample=f"{n} decode steps after a {PROMPT}-token prefill, batch {B}, Llama-3.2-1B Q8_0")
-
-
-def run_reference_gpu(args):
-    """The reference's own cuda.cu (oracle/_ref) through the Go-loop host mirror."""
-    import wukong_b200 as wk
-    from oracle import oracle as orc
-    from tests.model_util import DeviceModel, host_mirror
-    ref = ctypes.CDLL(orc.REF_LIB_PATH, mode=ctypes.RTLD_LOCAL)
-    ref.cuda_init.argtypes = [ctypes.c_int]
-    ref.cuda_init(0)
-    L = wk.lib()
-    L.cuda_init(0)
-    cfg = dict(CFG_1B)
-    B, K, W = args.batch, args.steps, args.warmup
-    ctx = PROMPT + W + K + 8
-    w = make_model_host(cfg, seed=1234)
-    dm = DeviceModel(w)
-    L.cuda_to_host(ctypes.byref(ctypes.c_int()), dm.freqs, 4)  # weights resident
-    h, _ = host_mirror(dm, cfg, 8, 8, 1, ctx, lib_handle=ref._handle)
-    prompt = np.random.default_rng(7).integers(0, cfg["V"], size=(B, PROMPT)).astype(np.int32)
-    seqs = [list(prompt[b]) for b in range(B)]
-    out = np.zeros(B, np.int32)
-
-    def step():
-        ids = np.ascontiguousarray(np.array(seqs, np.int32))
-        assert L.wk_host_llama_predict(h, ids.ctypes.data_as(ctypes.c_void_p), B, ids.shape[1],
-                                       out.ctypes.data_as(ctypes.c_void_p)) == 0
-        for b in range(B):
-            seqs[b].append(int(out[b]))
-
-    for _ in range(W + 1):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(K):
-        step()
-    dt = time.perf_counter() - t0
-    return B * K / dt
+                sample=f"{n} decode steps after a {P}-token prefill, batch {B}, {NAMES[model]} Q8_0")
 
 
 # ------------------------------------------------------------------ main
@@ -299,23 +351,42 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
+    ap.add_argument("--model", default="1b", choices=["1b", "8b", "70b"])
+    ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 128 / 2048 / 4096)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--op", default=None, metavar="NxKxM[,...]",
+                    help="time only the Q8_0 dequant-matmul op at these shapes (one JSON line each), "
+                         "e.g. 8192x2048x1,8192x2048x16,8192x2048x128")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.prompt is None:
+        args.prompt = PROMPTS[args.model]
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    cfg = dict(CFG_1B)
-    config = {"workload": f"Llama-3.2-1B Q8_0 greedy decode, batch {args.batch}, {PROMPT}-token prompt",
-              "batch": args.batch, "prompt": PROMPT, "decode_steps": args.steps, "weights": "Q8_0 (output Q8_0), "
-              "token_embd F16, norms 1.0, w ~ N(0, 0.02)", "l2": "per-step weights 1.31 GB > 126 MB L2, no flush",
-              "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    tp = args.model != "1b" and world > 1
+    if tp:
+        par = f"tp{world}"
+    elif world > 1:
+        par = f"replicas x{world}"
+    else:
+        par = "single GPU"
+    config = {"workload": f"{NAMES[args.model]} Q8_0 greedy decode, batch {args.batch}, {args.prompt}-token prompt",
+              "model": NAMES[args.model], "batch": args.batch, "prompt": args.prompt, "decode_steps": args.steps,
+              "weights": "Q8_0 linear layers and output.weight, token_embd F16, norms 1.0, w ~ N(0, 0.02), "
+                         "generated on the device",
+              "l2": "weights read per step exceed the 126 MB L2, no flush", "parallelism": par}
+
+    if args.op:
+        run_op(args.op)
+        return
 
     if args.impl == "reference":
         if rank != 0:
             return
-        cpu = run_cpu(cfg, args.batch, args.warmup + args.steps, budget_s=150.0)
+        cpu = run_cpu(args.model, args.batch, args.prompt, args.warmup + args.steps, budget_s=150.0)
         line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "n_gpus": 1,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "int8 x f16 -> f32",
                 "data": "synthetic", "config": config,
@@ -326,17 +397,12 @@ def main():
         print(json.dumps(line))
         return
 
-    if args.impl == "reference-gpu":
-        v = run_reference_gpu(args)
-        print(json.dumps({"impl": "reference-gpu", "metric": METRIC, "value": v, "unit": "tokens/s",
-                          "config": config, "path": "reference cuda.cu (sm_100a) via the llama.go call sequence, "
-                          "full re-prefill per step"}))
-        return
-
     if world > 1:
+        import datetime
         import torch
-        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", rank % torch.cuda.device_count()))
-    res = run_ours(args, rank, world)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                             timeout=datetime.timedelta(seconds=300))
+    res = run_ours(args, rank, world, local_rank)
     if world > 1:
         import torch
         torch.distributed.barrier()
@@ -345,25 +411,26 @@ def main():
         return
     hbm, src = peaks()
     K = args.steps
-    value = world * args.batch * K / (res["ms"] / 1e3)
+    value = (1 if tp else world) * args.batch * K / (res["ms"] / 1e3)
     g = res["gemv"]
+    gname = f"gemv_q8_0_{g['N']}x{g['K']}_m{g['M']}"
+    step_gbs = res["step_bytes"] / (res["ms"] / K) / 1e6
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
-        "ms_per_step": res["ms"] / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8 x f16 -> f32", "data": "synthetic", "config": config,
+        "ms_per_step": res["ms"] / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
+        "vs_baseline": None, "dtype": "int8 x f16 -> f32", "data": "synthetic", "config": config,
         "gpu_launches": res["launches"] * K,
         "roofline": {"bound": "hbm", "kernel": f"gemv_kernel<Q8_0> {g['N']}x{g['K']} M={g['M']}",
                      "achieved": g["gbs"], "peak": hbm, "unit": "GB/s", "frac": g["gbs"] / hbm,
-                     "peak_source": src, "traffic": None,
-                     "step": {"bytes": res["step_bytes"], "achieved": res["step_bytes"] / (res["ms"] / K) / 1e6,
-                              "frac": res["step_bytes"] / (res["ms"] / K) / 1e6 / hbm}},
+                     "peak_source": src, "traffic": profiled_traffic(gname),
+                     "step": {"bytes_per_gpu": res["step_bytes"], "achieved": step_gbs, "frac": step_gbs / hbm}},
         "op_gemv_8192x2048": res["gemv_op"],
         "clocks": res["clocks"],
     }
     if "e2e" in res:
         line["e2e"] = res["e2e"]
-    if not args.no_cpu and world == 1:
-        cpu = run_cpu(cfg, args.batch, 64)
+    if not args.no_cpu and world == 1 and args.model == "1b":
+        cpu = run_cpu(args.model, args.batch, args.prompt, 64)
         line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
     print(json.dumps(line))
 

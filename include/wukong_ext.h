@@ -75,6 +75,25 @@ int wk_gemv(void *out, const void *x, const void *w, int M, int K, int N, int wt
 /* library stream (cudaStream_t) so hosts can order their own work */
 void *wk_stream(void);
 
+/* Tensor parallelism inside one node, one process per GPU (no counterpart in
+ * the reference, which runs on one device): column-parallel q|k|v and up|gate,
+ * row-parallel o and down with an fp32 all-reduce after each, vocabulary-
+ * parallel logits with a winner exchange; NCCL is loaded at run time.
+ * Rank r of `world`: wk_tp_unique_id on one rank, share the 128 bytes, then
+ * wk_tp_init(r, world, id) on every rank after cuda_init.  A model made for TP
+ * holds the rank's shard: wk_config's n_heads, n_kv_heads, ffn and vocab are
+ * the per-rank counts (global / world); qkv = [q heads r*H..][k heads r*Hk..]
+ * [v heads r*Hk..] rows, o = the K-columns of those q heads, fc = [up rows
+ * r*F..][gate rows r*F..], down = the K-columns r*F.., output = vocabulary rows
+ * r*V..; embeddings and norms are whole.  Call wk_model_set_tp(m, 1) before
+ * wk_model_alloc_cache.  Every rank runs the same calls in the same order. */
+int wk_tp_unique_id(void *id);
+int wk_tp_init(int rank, int world, const void *id);
+void wk_tp_fini(void);
+int wk_tp_rank(void);
+int wk_tp_world(void);
+int wk_model_set_tp(wk_model *m, int enable);
+
 /* No counterpart in the reference.  cuda_predict without device allocation,
  * for hosts that cannot call cudaMalloc at that point: a process that has
  * given all free HBM to its own KV-cache pool, or a latency-critical loop in

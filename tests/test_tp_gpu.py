@@ -1,0 +1,111 @@
+"""Tensor-parallel engine on 2 GPUs against the single-GPU engine.
+
+Two child processes (one per GPU) shard a small Q8_0 Llama with
+wukong_b200.tp, join one NCCL communicator through wk_tp_init and run prefill
+(tcgen05 GEMM path, 48 rows) and greedy decode steps (GEMV path) with the
+row-parallel partial sums, the fp32 all-reduce and the vocabulary-parallel
+argmax exchange.  Their tokens must equal those of the unsharded engine on the
+same weights.  Skipped on a box with fewer than 2 GPUs.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import wukong_b200 as wk
+
+pytestmark = pytest.mark.gpu
+CFG = dict(L=2, d=512, H=8, Hk=4, D=64, F=1024, V=4096, eps=1e-5, theta=500000.0)
+B, P, STEPS, CTX = 2, 24, 8, 64
+
+
+def _model():
+    from tests.model_util import make_weights
+    return make_weights(CFG, wk.Q8_0, wk.Q8_0, wk.F16, seed=515, ctx=CTX)
+
+
+def _run(engine_cfg, layers, w, tp):
+    """Prefill + STEPS greedy steps; returns the tokens of each call."""
+    from tests.gpu_util import down, up
+    from wukong_b200.engine import Engine
+    L = wk.lib()
+    ptrs = [up(w["token_embd"]), up(w["output_norm"]), up(w["output"]), up(w["freqs"])]
+    eng = Engine(engine_cfg, layers, ptrs[0], ptrs[1], ptrs[2], ptrs[3], CTX, max_batch=B, tp=tp)
+    prompt = np.random.default_rng(3).integers(0, CFG["V"], size=(B, P)).astype(np.int32)
+    dp = up(prompt)
+    toks = []
+    eng.prefill(dp, B, P)
+    toks.append(down(eng.tokens_ptr(), B, np.int32).tolist())
+    for _ in range(STEPS):
+        eng.step()
+        toks.append(down(eng.tokens_ptr(), B, np.int32).tolist())
+    eng.destroy()
+    for p in ptrs + [dp]:
+        L.cuda_free(p)
+    return toks
+
+
+def _worker(rank, world, uid, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        from tests.gpu_util import up
+        from wukong_b200 import tp
+        L = wk.lib()
+        L.cuda_init(rank)
+        wk.check(L.wk_tp_init(rank, world, uid))
+        w = _model()
+        layers = []
+        for lw in w["layers"]:
+            s = tp.shard_layer(lw, CFG, wk.Q8_0, rank, world)
+            layers.append({k: up(v) for k, v in s.items()})
+        wo = dict(w, output=tp.shard_output(w["output"], CFG, wk.Q8_0, rank, world))
+        toks = _run(tp.local_config(CFG, world), layers, wo, tp=True)
+        L.wk_tp_fini()
+        q.put((rank, toks))
+    except Exception as e:  # reported to the parent
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+def test_tp2_engine_matches_single_gpu(dev):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs 2 GPUs")
+    import torch.multiprocessing as mp
+    from tests.gpu_util import up
+    uid = ctypes.create_string_buffer(128)
+    wk.check(dev.wk_tp_unique_id(uid))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, uid.raw, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        # poll, so that a child that dies without reporting fails the test at once
+        import queue
+        import time
+        t0 = time.time()
+        while len(got) < len(procs) and time.time() - t0 < 240:
+            try:
+                r, v = q.get(timeout=2)
+                got[r] = v
+            except queue.Empty:
+                dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+                if dead and q.empty():
+                    break
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    # the unsharded engine on the same weights, in this process (cuda:0)
+    w = _model()
+    from tests.model_util import fused_for_oracle
+    layers = [{k: up(v) for k, v in lw.items()} for lw in fused_for_oracle(w)["layers"]]
+    ref = _run(CFG, layers, w, tp=False)
+    assert set(got) == {0, 1}, f"ranks reported {sorted(got)}; exit codes {[p.exitcode for p in procs]}"
+    assert isinstance(got[0], list), got[0]
+    assert isinstance(got[1], list), got[1]
+    assert got[0] == got[1]
+    assert got[0] == ref

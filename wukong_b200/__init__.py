@@ -70,6 +70,12 @@ EXT = {
     "wk_fill_const_f32": (_I, [_P, _L, _F]),
     "wk_gemv": (_I, [_P, _P, _P, _I, _I, _I, _I]),
     "wk_predict_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _F, _I]),
+    "wk_tp_unique_id": (_I, [_P]),
+    "wk_tp_init": (_I, [_I, _I, _P]),
+    "wk_tp_fini": (None, []),
+    "wk_tp_rank": (_I, []),
+    "wk_tp_world": (_I, []),
+    "wk_model_set_tp": (_I, [_P, _I]),
 }
 
 

@@ -231,4 +231,70 @@ __device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, __half2 &lo, __half2 &h
 }
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
 
+// Argmax order of the reference's argmax kernel (cuda.cu:480-531) as a sort key:
+// element idx of a row is read by thread (idx / pack) % 256 in iteration
+// (idx / pack) / 256 as the (idx % pack)-th value of a packed load; ties go to the
+// first iteration within a thread, then to the lane / warp with the smaller
+// bit-reversed index (the shfl_down tree).  Smaller key = preferred on ties.
+__device__ __forceinline__ uint64_t logits_key(long idx, int pack) {
+    const long p = idx / pack;
+    const uint32_t tid = (uint32_t)(p & 255), j = (uint32_t)(p >> 8), e = (uint32_t)(idx - p * pack);
+    const uint32_t bw = __brev(tid >> 5) >> 27, bl = __brev(tid & 31) >> 27;
+    return ((uint64_t)bw << 58) | ((uint64_t)bl << 53) | ((uint64_t)j << 8) | e;
+}
+// Inverse of logits_key (-1 for the empty key ~0).
+__device__ __forceinline__ int logits_index(uint64_t key, int pack) {
+    if (key == ~0ull) return -1;
+    const uint32_t bw = (uint32_t)(key >> 58) & 31, bl = (uint32_t)(key >> 53) & 31;
+    const uint32_t tid8 = ((__brev(bw) >> 27) << 5) | (__brev(bl) >> 27);
+    const long j = (long)((key >> 8) & ((1ull << 45) - 1));
+    return (int)(((j << 8) + tid8) * pack + (int)(key & 255));
+}
+
+// One Q8_0 block (32 k, two MMA k-slices) of rows g and g + 8 of the staged tile:
+// lane t takes quant bytes 4t..4t+3 of each 16-value half.  Odd blocks start
+// their quants 4-byte aligned (34 * odd + 2 = 0 mod 4); even ones are realigned
+// by a byte permute of two neighbouring words.
+__device__ __forceinline__ void q8_block(const uint8_t *r0, const uint8_t *r1, int off, bool odd, int t, uint2 x0,
+                                         uint2 x1, float (&c)[2][4]) {
+    const __half2 s0 = __half2half2(*reinterpret_cast<const __half *>(r0 + off));
+    const __half2 s1 = __half2half2(*reinterpret_cast<const __half *>(r1 + off));
+    uint32_t q0[2], q1[2];  // [slice] quant words for rows g, g+8
+    if (odd) {
+        q0[0] = *reinterpret_cast<const uint32_t *>(r0 + off + 2 + 4 * t);
+        q0[1] = *reinterpret_cast<const uint32_t *>(r0 + off + 18 + 4 * t);
+        q1[0] = *reinterpret_cast<const uint32_t *>(r1 + off + 2 + 4 * t);
+        q1[1] = *reinterpret_cast<const uint32_t *>(r1 + off + 18 + 4 * t);
+    } else {
+        const uint32_t *p0 = reinterpret_cast<const uint32_t *>(r0 + off + 4 * t);
+        const uint32_t *p1 = reinterpret_cast<const uint32_t *>(r1 + off + 4 * t);
+        q0[0] = __byte_perm(p0[0], p0[1], 0x5432);
+        q0[1] = __byte_perm(p0[4], p0[5], 0x5432);
+        q1[0] = __byte_perm(p1[0], p1[1], 0x5432);
+        q1[1] = __byte_perm(p1[4], p1[5], 0x5432);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        __half2 lo0, hi0, lo1, hi1;
+        i8x4_to_h2x2(q0[h], lo0, hi0);
+        i8x4_to_h2x2(q1[h], lo1, hi1);
+        const uint32_t a0 = h2_as_u32(__hmul2(lo0, s0)), a2 = h2_as_u32(__hmul2(hi0, s0));
+        const uint32_t a1 = h2_as_u32(__hmul2(lo1, s1)), a3 = h2_as_u32(__hmul2(hi1, s1));
+        const uint2 xv = h ? x1 : x0;
+        mma_f16(c[h], a0, a1, a2, a3, xv.x, xv.y);
+    }
+}
+
+// ldmatrix: four 8x8 b16 tiles (optionally transposed) from shared memory
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
 }  // namespace wk

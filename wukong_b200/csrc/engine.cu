@@ -174,6 +174,11 @@ struct wk_model {
     // activations
     int rows_cap = 0;
     void *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
+    void *xn = nullptr;  // RMSNorm output when a linear layer runs on the tcgen05 GEMM
+    // tensor parallelism: this model holds one rank's shard (wk_model_set_tp)
+    int tp = 0;
+    float *p32 = nullptr;                           // [rows_cap, d] fp32 partials of o / down
+    void *win_send = nullptr, *win_recv = nullptr;  // logits winners of this rank / of all ranks
     // logits argmax partials
     float *part_val = nullptr;
     unsigned long long *part_key = nullptr;
@@ -190,7 +195,7 @@ int ensure_rows(wk_model *m, int rows) {
     const wk_config &c = m->cfg;
     const size_t es = act_size(m->act);
     cudaStream_t s = stream();
-    for (void **p : {&m->x, &m->q, &m->att, &m->h})
+    for (void **p : {&m->x, &m->q, &m->att, &m->h, &m->xn})
         if (*p) WK_TRY(cudaFreeAsync(*p, s));
     for (int **p : {&m->d_row_seq, &m->d_row_pos})
         if (*p) WK_TRY(cudaFreeAsync(*p, s));
@@ -198,10 +203,27 @@ int ensure_rows(wk_model *m, int rows) {
     WK_TRY(cudaMallocAsync(&m->q, es * rows * c.n_heads * c.head_dim, s));
     WK_TRY(cudaMallocAsync(&m->att, es * rows * c.n_heads * c.head_dim, s));
     WK_TRY(cudaMallocAsync(&m->h, es * rows * c.ffn, s));
+    WK_TRY(cudaMallocAsync(&m->xn, es * rows * c.d_model, s));
+    if (m->tp) {
+        if (m->p32) WK_TRY(cudaFreeAsync(m->p32, s));
+        WK_TRY(cudaMallocAsync(&m->p32, sizeof(float) * rows * c.d_model, s));
+    }
     WK_TRY(cudaMallocAsync(&m->d_row_seq, sizeof(int) * rows, s));
     WK_TRY(cudaMallocAsync(&m->d_row_pos, sizeof(int) * rows, s));
     m->rows_cap = rows;
     return 0;
+}
+
+// Tensor parallelism: sum the o / down partials of all ranks and add them to
+// the residual stream.  Returns the number of this library's kernel launches.
+int reduce_partials(wk_model *m, int rows, cudaStream_t s) {
+    const long n = (long)rows * m->cfg.d_model;
+    tp_allreduce_f32(m->p32, (size_t)n, s);
+    if (m->act == kF16)
+        resid_from_partial<__half>((__half *)m->x, m->p32, n, s);
+    else
+        resid_from_partial<__nv_bfloat16>((__nv_bfloat16 *)m->x, m->p32, n, s);
+    return 1;
 }
 
 // Run the layers and the logits head on `rows` activation rows in m->x.
@@ -220,9 +242,10 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
     kv.kv_heads = c.n_kv_heads;
     kv.hd = c.head_dim;
     int launches = 0;
-    // L2 prefetch plan: every kernel streams the weights of a later kernel
-    // (qkv -> o, attention -> fc, o -> down, fc -> next qkv, down -> next fc;
-    // the last layer prefetches the head of the logits matrix)
+    // L2 prefetch plan: each linear layer streams the weights of the next one
+    // (qkv -> o, o -> fc, fc -> down, down -> next qkv); the last down
+    // prefetches the head of the logits matrix.  Attention prefetches nothing
+    // (its few CTAs would queue the prefetches ahead of their own page loads).
     auto wbytes = [&](long rows, int K, int wt) -> long {
         return wt == kQ8_0 ? rows * (K / 32) * 34 : rows * (long)K * 2;
     };
@@ -234,106 +257,107 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
         const bool last = l + 1 == c.n_layers;
         kv.k = m->kpool[l];
         kv.v = m->vpool[l];
-        for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
+        {
             GemvArgs a;
             a.w = L.qkv;
             a.wtype = c.wtype;
-            a.N = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+            a.N = W;
             a.K = d;
-            a.x = (const char *)m->x + (size_t)m0 * d * es;
+            a.x = m->x;
             a.ldx = d;
-            a.M = rows - m0 < 8 ? rows - m0 : 8;
             a.norm_w = L.attn_norm;
             a.eps = c.eps;
             a.epi = EPI_QKV;
-            a.out = (char *)m->q + (size_t)m0 * col * es;
+            a.out = m->q;
             a.ldo = col;
             a.nq = c.n_heads * c.head_dim;
             a.nk = c.n_kv_heads * c.head_dim;
             a.hd = c.head_dim;
             a.freqs = m->freqs;
-            a.pos = pos + m0;
-            a.seq = seq + m0;
+            a.pos = pos;
+            a.seq = seq;
             a.kpool = kv.k;
             a.vpool = kv.v;
             a.block_table = kv.block_table;
             a.max_pages = kv.max_pages;
             a.page = kPage;
             a.kv_heads = c.n_kv_heads;
-            if (m0 == 0) {
-                a.pf = L.o;
-                a.pf_bytes = wbytes(d, col, c.wtype);
-            }
-            gemv(a, m->act, s);
+            a.pf = L.o;
+            a.pf_bytes = wbytes(d, col, c.wtype);
+            launches += linear(a, rows, m->act, s, m->xn);
         }
         if (m->act == kF16)
             attention_paged<__half>((__half *)m->att, col, (const __half *)m->q, col, seq, pos, rows, max_len, kv,
-                                    c.n_heads, s, true, L.fc, wbytes(2L * c.ffn, d, c.wtype));
+                                    c.n_heads, s, true);
         else
             attention_paged<__nv_bfloat16>((__nv_bfloat16 *)m->att, col, (const __nv_bfloat16 *)m->q, col, seq, pos,
-                                           rows, max_len, kv, c.n_heads, s, true, L.fc,
-                                           wbytes(2L * c.ffn, d, c.wtype));
+                                           rows, max_len, kv, c.n_heads, s, true);
         ++launches;
-        for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
+        {
             GemvArgs a;
             a.w = L.o;
             a.wtype = c.wtype;
             a.N = d;
             a.K = col;
-            a.x = (const char *)m->att + (size_t)m0 * col * es;
+            a.x = m->att;
             a.ldx = col;
-            a.M = rows - m0 < 8 ? rows - m0 : 8;
-            a.epi = EPI_RESID;
-            a.out = (char *)m->x + (size_t)m0 * d * es;
-            a.ldo = d;
-            a.res = a.out;
-            a.ldr = d;
-            if (m0 == 0) {
-                a.pf = L.down;
-                a.pf_bytes = wbytes(d, c.ffn, c.wtype);
+            if (m->tp) {
+                a.epi = EPI_PARTIAL;
+                a.out = m->p32;
+                a.ldo = d;
+            } else {
+                a.epi = EPI_RESID;
+                a.out = m->x;
+                a.ldo = d;
+                a.res = m->x;
+                a.ldr = d;
             }
-            gemv(a, m->act, s);
+            a.pf = L.fc;
+            a.pf_bytes = wbytes(2L * c.ffn, d, c.wtype) / 2;
+            launches += linear(a, rows, m->act, s, nullptr);
+            if (m->tp) launches += reduce_partials(m, rows, s);
         }
-        for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
+        {
             GemvArgs a;
             a.w = L.fc;
             a.wtype = c.wtype;
             a.N = 2 * c.ffn;
             a.K = d;
-            a.x = (const char *)m->x + (size_t)m0 * d * es;
+            a.x = m->x;
             a.ldx = d;
-            a.M = rows - m0 < 8 ? rows - m0 : 8;
             a.norm_w = L.ffn_norm;
             a.eps = c.eps;
             a.epi = EPI_SWIGLU;
             a.F = c.ffn;
-            a.out = (char *)m->h + (size_t)m0 * c.ffn * es;
+            a.out = m->h;
             a.ldo = c.ffn;
-            if (m0 == 0) {
-                a.pf = last ? (const void *)m->out_w : (const void *)m->layers[l + 1].qkv;
-                a.pf_bytes = last ? logit_pf / 2 : wbytes(W, d, c.wtype);
-            }
-            gemv(a, m->act, s);
+            a.pf = L.down;
+            a.pf_bytes = wbytes(d, c.ffn, c.wtype);
+            launches += linear(a, rows, m->act, s, m->xn);
         }
-        for (int m0 = 0; m0 < rows; m0 += 8, ++launches) {
+        {
             GemvArgs a;
             a.w = L.down;
             a.wtype = c.wtype;
             a.N = d;
             a.K = c.ffn;
-            a.x = (const char *)m->h + (size_t)m0 * c.ffn * es;
+            a.x = m->h;
             a.ldx = c.ffn;
-            a.M = rows - m0 < 8 ? rows - m0 : 8;
-            a.epi = EPI_RESID;
-            a.out = (char *)m->x + (size_t)m0 * d * es;
-            a.ldo = d;
-            a.res = a.out;
-            a.ldr = d;
-            if (m0 == 0) {
-                a.pf = last ? (const char *)m->out_w + logit_pf / 2 : (const void *)m->layers[l + 1].fc;
-                a.pf_bytes = last ? logit_pf / 2 : wbytes(2L * c.ffn, d, c.wtype);
+            if (m->tp) {
+                a.epi = EPI_PARTIAL;
+                a.out = m->p32;
+                a.ldo = d;
+            } else {
+                a.epi = EPI_RESID;
+                a.out = m->x;
+                a.ldo = d;
+                a.res = m->x;
+                a.ldr = d;
             }
-            gemv(a, m->act, s);
+            a.pf = last ? (const void *)m->out_w : (const void *)m->layers[l + 1].qkv;
+            a.pf_bytes = last ? logit_pf : wbytes(W, d, c.wtype);
+            launches += linear(a, rows, m->act, s, nullptr);
+            if (m->tp) launches += reduce_partials(m, rows, s);
         }
     }
     // logits + argmax on the last row of each sequence
@@ -352,21 +376,35 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
         a.part_val = m->part_val;
         a.part_key = m->part_key;
         a.counter = m->counter;
-        a.tokens = tokens + b0;
         a.pack = 16 / (int)es;
+        if (m->tp) {
+            // vocabulary shard: keys in whole-vocabulary columns, winners exchanged below
+            a.col_off = (long)tp_rank() * c.vocab;
+            a.n_total = c.vocab * tp_world();
+            a.best_key = (unsigned long long *)m->win_send + b0;
+            a.best_val = (float *)((char *)m->win_send + 8L * batch) + b0;
+        } else {
+            a.tokens = tokens + b0;
+        }
         gemv(a, m->act, s);
+    }
+    if (m->tp) {
+        tp_argmax_combine(tokens, m->win_send, m->win_recv, batch, 16 / (int)es, s);
+        ++launches;
     }
     return launches;
 }
 
 void launch_embed(wk_model *m, const int *ids, int rows) {
     const wk_config &c = m->cfg;
+    // the token table is whole on every rank; a shard's vocab counts only its logits rows
+    const int vocab = m->tp ? c.vocab * tp_world() : c.vocab;
     if (m->act == kF16)
         embed_kernel<__half><<<rows, 256, 0, stream()>>>((__half *)m->x, ids, m->embd, c.d_model, c.embd_wtype,
-                                                         c.vocab, g_rt.d_error);
+                                                         vocab, g_rt.d_error);
     else
         embed_kernel<__nv_bfloat16><<<rows, 256, 0, stream()>>>((__nv_bfloat16 *)m->x, ids, m->embd, c.d_model,
-                                                                c.embd_wtype, c.vocab, g_rt.d_error);
+                                                                c.embd_wtype, vocab, g_rt.d_error);
     WK_CHECK_LAUNCH();
 }
 
@@ -385,7 +423,9 @@ wk_model *wk_model_create(const wk_config *cfg) {
     }
     set_device_current();
     const wk_config &c = *cfg;
-    if (c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads || c.n_heads * c.head_dim != c.d_model || c.head_dim % 2) {
+    // n_heads * head_dim is d_model, or d_model / world for a tensor-parallel shard
+    if (c.n_kv_heads <= 0 || c.n_heads <= 0 || c.n_heads % c.n_kv_heads || c.head_dim % 2 ||
+        c.d_model % (c.n_heads * c.head_dim)) {
         fail("inconsistent attention geometry");
         return nullptr;
     }
@@ -425,7 +465,8 @@ void wk_model_destroy(wk_model *m) {
     free(m->kpool);
     free(m->vpool);
     void *bufs[] = {m->block_table, m->d_pos, m->d_seq, m->d_ids, m->d_tokens, m->d_row_seq, m->d_row_pos,
-                    m->x, m->q, m->att, m->h, m->part_val, m->part_key, m->counter};
+                    m->x, m->q, m->att, m->h, m->xn, m->part_val, m->part_key, m->counter,
+                    m->p32, m->win_send, m->win_recv};
     for (void *p : bufs)
         if (p) cudaFree(p);
     free(m->layers);
@@ -476,6 +517,18 @@ int wk_model_alloc_cache(wk_model *m, int max_batch, int max_ctx) {
     for (int **p : {&m->d_pos, &m->d_seq, &m->d_ids, &m->d_tokens}) WK_TRY(cudaMallocAsync(p, sizeof(int) * max_batch, s));
     iota_kernel<<<(max_batch + 127) / 128, 128, 0, s>>>(m->d_seq, max_batch, 0, 1);
     WK_TRY(cudaGetLastError());
+    if (m->tp) {
+        WK_TRY(cudaMallocAsync(&m->win_send, tp_winner_chunk(max_batch), s));
+        WK_TRY(cudaMallocAsync(&m->win_recv, tp_winner_chunk(max_batch) * tp_world(), s));
+    }
+    return 0;
+}
+
+int wk_model_set_tp(wk_model *m, int enable) {
+    if (!m) return fail("null model");
+    if (m->kpool) return fail("wk_model_set_tp must come before wk_model_alloc_cache");
+    if (enable && !tp_active()) return fail("wk_model_set_tp: wk_tp_init has not set up more than one rank");
+    m->tp = enable ? 1 : 0;
     return 0;
 }
 

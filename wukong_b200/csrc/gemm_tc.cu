@@ -157,6 +157,10 @@ __device__ __forceinline__ void store_out(const GemmArgs &a, int n, int m, float
         reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(acc);
         break;
     }
+    case EPI_PARTIAL: {
+        reinterpret_cast<float *>(a.out)[(long)m * a.ldo + n] = acc;
+        break;
+    }
     case EPI_RESID: {
         const float y = round_to<T>(acc);
         const float rv = to_float(reinterpret_cast<const T *>(a.res)[(long)m * a.ldr + n]);

@@ -137,40 +137,6 @@ __device__ __forceinline__ void produce_unit(const GemvArgs &a, const Smem &sm, 
     }
 }
 
-// One Q8_0 block (32 k, two MMA k-slices) of rows g and g + 8 of the staged tile:
-// lane t takes quant bytes 4t..4t+3 of each 16-value half.  Odd blocks start
-// their quants 4-byte aligned (34 * odd + 2 = 0 mod 4); even ones are realigned
-// by a byte permute of two neighbouring words.
-__device__ __forceinline__ void q8_block(const uint8_t *r0, const uint8_t *r1, int off, bool odd, int t, uint2 x0,
-                                         uint2 x1, float (&c)[2][4]) {
-    const __half2 s0 = __half2half2(*reinterpret_cast<const __half *>(r0 + off));
-    const __half2 s1 = __half2half2(*reinterpret_cast<const __half *>(r1 + off));
-    uint32_t q0[2], q1[2];  // [slice] quant words for rows g, g+8
-    if (odd) {
-        q0[0] = *reinterpret_cast<const uint32_t *>(r0 + off + 2 + 4 * t);
-        q0[1] = *reinterpret_cast<const uint32_t *>(r0 + off + 18 + 4 * t);
-        q1[0] = *reinterpret_cast<const uint32_t *>(r1 + off + 2 + 4 * t);
-        q1[1] = *reinterpret_cast<const uint32_t *>(r1 + off + 18 + 4 * t);
-    } else {
-        const uint32_t *p0 = reinterpret_cast<const uint32_t *>(r0 + off + 4 * t);
-        const uint32_t *p1 = reinterpret_cast<const uint32_t *>(r1 + off + 4 * t);
-        q0[0] = __byte_perm(p0[0], p0[1], 0x5432);
-        q0[1] = __byte_perm(p0[4], p0[5], 0x5432);
-        q1[0] = __byte_perm(p1[0], p1[1], 0x5432);
-        q1[1] = __byte_perm(p1[4], p1[5], 0x5432);
-    }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        __half2 lo0, hi0, lo1, hi1;
-        i8x4_to_h2x2(q0[h], lo0, hi0);
-        i8x4_to_h2x2(q1[h], lo1, hi1);
-        const uint32_t a0 = h2_as_u32(__hmul2(lo0, s0)), a2 = h2_as_u32(__hmul2(hi0, s0));
-        const uint32_t a1 = h2_as_u32(__hmul2(lo1, s1)), a3 = h2_as_u32(__hmul2(hi1, s1));
-        const uint2 xv = h ? x1 : x0;
-        mma_f16(c[h], a0, a1, a2, a3, xv.x, xv.y);
-    }
-}
-
 // Consume one unit: accumulate the 16 x 8 tile over the chunk's k-slices into
 // two independent accumulators (even / odd slice) to halve the MMA chain.
 template <int WT>
@@ -272,13 +238,6 @@ __device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad) {
     }
 }
 
-__device__ __forceinline__ uint64_t logits_key(long idx, int pack) {
-    const long p = idx / pack;
-    const uint32_t tid = (uint32_t)(p & 255), j = (uint32_t)(p >> 8), e = (uint32_t)(idx - p * pack);
-    const uint32_t bw = __brev(tid >> 5) >> 27, bl = __brev(tid & 31) >> 27;
-    return ((uint64_t)bw << 58) | ((uint64_t)bl << 53) | ((uint64_t)j << 8) | e;
-}
-
 // Threads 0..127 own one (row r, column m) output of the 16 x 8 tile.
 template <typename T>
 __device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float &best_v, uint64_t &best_k) {
@@ -340,12 +299,18 @@ __device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float &bes
         }
         break;
     }
+    case EPI_PARTIAL: {
+        reinterpret_cast<float *>(a.out)[(long)m * a.ldo + n] = acc;
+        break;
+    }
     case EPI_LOGITS: {
         const float y = round_to<T>(acc);
         if (a.out) reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(y);
-        const long lim = (long)(a.N / a.pack) * a.pack;
-        if (n < lim && (y > best_v || (y == best_v && best_k != ~0ull))) {
-            const uint64_t k = logits_key(n, a.pack);
+        // keys and the reference's row cut-off use the column in the whole vocabulary
+        const long gn = (long)n + a.col_off;
+        const long lim = (long)((a.n_total ? a.n_total : a.N) / a.pack) * a.pack;
+        if (gn < lim && (y > best_v || (y == best_v && best_k != ~0ull))) {
+            const uint64_t k = logits_key(gn, a.pack);
             if (y > best_v || k < best_k) {
                 best_v = y;
                 best_k = k;
@@ -477,14 +442,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
                         bk = ok;
                     }
                 }
-                int idx = -1;
-                if (bk != ~0ull) {
-                    const uint32_t bw = (uint32_t)(bk >> 58) & 31, bl = (uint32_t)(bk >> 53) & 31;
-                    const uint32_t tid8 = ((__brev(bw) >> 27) << 5) | (__brev(bl) >> 27);
-                    const long j = (long)((bk >> 8) & ((1ull << 45) - 1));
-                    idx = (int)(((j << 8) + tid8) * a.pack + (int)(bk & 255));
+                if (a.tokens) a.tokens[tid] = logits_index(bk, a.pack);
+                if (a.best_val) {
+                    a.best_val[tid] = bv;
+                    a.best_key[tid] = bk;
                 }
-                a.tokens[tid] = idx;
             }
             if (tid == 0) *a.counter = 0;
         }
@@ -555,11 +517,15 @@ void gemv(GemvArgs a, int act, cudaStream_t s) {
         b.M = a.M - m1;
         a.M = m1;
         b.x = (const char *)a.x + (size_t)m1 * a.ldx * es;
-        if (b.epi != EPI_LOGITS) b.out = (char *)a.out + (size_t)m1 * a.ldo * es;
+        if (b.epi != EPI_LOGITS) b.out = (char *)a.out + (size_t)m1 * a.ldo * (b.epi == EPI_PARTIAL ? 4 : es);
         if (b.res) b.res = (const char *)a.res + (size_t)m1 * a.ldr * es;
         if (b.pos) b.pos += m1;
         if (b.seq) b.seq += m1;
         if (b.tokens) b.tokens += m1;
+        if (b.best_val) {
+            b.best_val += m1;
+            b.best_key += m1;
+        }
         if (b.epi == EPI_LOGITS && b.out) b.out = (char *)a.out + (size_t)m1 * a.ldo * es;
         gemv(a, act, s);
         gemv(b, act, s);

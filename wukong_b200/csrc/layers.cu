@@ -199,7 +199,7 @@ void gqa_fused(void *out, const void *embeds, const float *freqs, const float *n
     kv.page = kPage;
     kv.kv_heads = kvNH;
     kv.hd = HS;
-    size_t need = Carver::round(sizeof(int) * rows) * 2 + Carver::round((size_t)rows * col * es) * 3;
+    size_t need = Carver::round(sizeof(int) * rows) * 2 + Carver::round((size_t)rows * col * es) * 4;
     if (r.cached) {
         if (g_sess.kv_heads != kvNH || g_sess.hd != HS || g_sess.act != act)
             WK_PANIC("prefix cache: attention geometry changed within a session");
@@ -219,6 +219,7 @@ void gqa_fused(void *out, const void *embeds, const float *freqs, const float *n
     char *q = c.take<char>((size_t)rows * col * es);
     char *att = c.take<char>((size_t)rows * col * es);
     char *xg = c.take<char>((size_t)rows * col * es);
+    char *xn = c.take<char>((size_t)rows * col * es);  // normalised rows for the tcgen05 GEMM
     if (!r.cached) {
         int *bt = c.take<int>((size_t)batch * kv.max_pages);
         fill_block_table(bt, batch, kv.max_pages, stream());
@@ -229,54 +230,52 @@ void gqa_fused(void *out, const void *embeds, const float *freqs, const float *n
     fill_row_meta(seq, pos, rows, r.n, r.P, stream());
     void *x = gather_new_rows(out, batch, row, col, r.P, es, xg);
 
-    for (int m0 = 0; m0 < rows; m0 += 8) {
+    {
         GemvArgs a;
         a.w = (const uint8_t *)qkv_w;
         a.wtype = wtype;
         a.N = W;
         a.K = col;
-        a.x = (const char *)x + (size_t)m0 * col * es;
+        a.x = x;
         a.ldx = col;
-        a.M = rows - m0 < 8 ? rows - m0 : 8;
         a.norm_w = norm_w;
         a.eps = eps;
         a.epi = EPI_QKV;
-        a.out = q + (size_t)m0 * col * es;
+        a.out = q;
         a.ldo = col;
         a.nq = NH * HS;
         a.nk = kvNH * HS;
         a.hd = HS;
         a.freqs = freqs;
-        a.pos = pos + m0;
-        a.seq = seq + m0;
+        a.pos = pos;
+        a.seq = seq;
         a.kpool = kv.k;
         a.vpool = kv.v;
         a.block_table = kv.block_table;
         a.max_pages = kv.max_pages;
         a.page = kPage;
         a.kv_heads = kvNH;
-        gemv(a, act, stream());
+        linear(a, rows, act, stream(), xn);
     }
     if (act == kF16)
         attention_paged<__half>((__half *)att, col, (const __half *)q, col, seq, pos, rows, row, kv, NH, stream(), true);
     else
         attention_paged<__nv_bfloat16>((__nv_bfloat16 *)att, col, (const __nv_bfloat16 *)q, col, seq, pos, rows, row,
                                        kv, NH, stream(), true);
-    for (int m0 = 0; m0 < rows; m0 += 8) {
+    {
         GemvArgs a;
         a.w = (const uint8_t *)out_w;
         a.wtype = wtype;
         a.N = col;
         a.K = col;
-        a.x = att + (size_t)m0 * col * es;
+        a.x = att;
         a.ldx = col;
-        a.M = rows - m0 < 8 ? rows - m0 : 8;
         a.epi = EPI_RESID;
-        a.out = (char *)x + (size_t)m0 * col * es;
+        a.out = x;
         a.ldo = col;
-        a.res = a.out;
+        a.res = x;
         a.ldr = col;
-        gemv(a, act, stream());
+        linear(a, rows, act, stream(), nullptr);
     }
     scatter_new_rows(out, x, batch, row, col, r.P, es);
     if (L) L->valid = row;
@@ -308,42 +307,41 @@ void ffn_fused(void *out, const void *attn, const float *norm_w, const void *fc_
         WK_CHECK(cudaMemcpyAsync(out, attn, (size_t)batch * row * col * es, cudaMemcpyDeviceToDevice, stream()));
     Rows r = plan_rows(out, batch, row);
     const int rows = batch * r.n;
-    Carver c(scratch(Carver::round((size_t)rows * ffl * es) + Carver::round((size_t)rows * col * es)));
+    Carver c(scratch(Carver::round((size_t)rows * ffl * es) + Carver::round((size_t)rows * col * es) * 2));
     char *h = c.take<char>((size_t)rows * ffl * es);
     char *xg = c.take<char>((size_t)rows * col * es);
+    char *xn = c.take<char>((size_t)rows * col * es);  // normalised rows for the tcgen05 GEMM
     void *x = gather_new_rows(out, batch, row, col, r.P, es, xg);
-    for (int m0 = 0; m0 < rows; m0 += 8) {
+    {
         GemvArgs a;
         a.w = (const uint8_t *)fc_w;
         a.wtype = wtype;
         a.N = 2 * ffl;
         a.K = col;
-        a.x = (const char *)x + (size_t)m0 * col * es;
+        a.x = x;
         a.ldx = col;
-        a.M = rows - m0 < 8 ? rows - m0 : 8;
         a.norm_w = norm_w;
         a.eps = eps;
         a.epi = EPI_SWIGLU;
         a.F = ffl;
-        a.out = h + (size_t)m0 * ffl * es;
+        a.out = h;
         a.ldo = ffl;
-        gemv(a, act, stream());
+        linear(a, rows, act, stream(), xn);
     }
-    for (int m0 = 0; m0 < rows; m0 += 8) {
+    {
         GemvArgs a;
         a.w = (const uint8_t *)down_w;
         a.wtype = wtype;
         a.N = col;
         a.K = ffl;
-        a.x = h + (size_t)m0 * ffl * es;
+        a.x = h;
         a.ldx = ffl;
-        a.M = rows - m0 < 8 ? rows - m0 : 8;
         a.epi = EPI_RESID;
-        a.out = (char *)x + (size_t)m0 * col * es;
+        a.out = x;
         a.ldo = col;
-        a.res = a.out;
+        a.res = x;
         a.ldr = col;
-        gemv(a, act, stream());
+        linear(a, rows, act, stream(), nullptr);
     }
     scatter_new_rows(out, x, batch, row, col, r.P, es);
 }

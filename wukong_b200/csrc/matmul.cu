@@ -171,6 +171,83 @@ void matmul(void *out, const void *x, const void *w, const void *bias, int M, in
     }
 }
 
+int linear(const GemvArgs &g, int rows, int act, cudaStream_t s, void *norm_scratch) {
+    if (rows <= 0) return 0;
+    const size_t es = act_size(act);
+    const bool tc = rows >= kTcMinRows && g_rt.tc_gemm && g.epi != EPI_LOGITS &&
+                    gemm_tc_supported(g.wtype, act, g.K, g.N, g.epi, g.F) && ((uintptr_t)g.w % 16) == 0 &&
+                    (g.wtype != kQ8_0 || ((size_t)(g.K / 32) * 34) % 16 == 0) &&
+                    (!g.norm_w || (norm_scratch && g.ldx == g.K && ((uintptr_t)norm_scratch % 16) == 0)) &&
+                    (g.norm_w || (((uintptr_t)g.x % 16) == 0 && ((size_t)g.ldx * es) % 16 == 0));
+    if (tc) {
+        GemmArgs a;
+        a.w = g.w;
+        a.wtype = g.wtype;
+        a.N = g.N;
+        a.K = g.K;
+        a.x = g.x;
+        a.ldx = g.ldx;
+        int n = 0;
+        if (g.norm_w) {
+            // the GEMM reads the normalised rows (same rounding as the GEMV prologue)
+            if (act == kBF16)
+                rmsnorm<__nv_bfloat16>((__nv_bfloat16 *)norm_scratch, (const __nv_bfloat16 *)g.x, g.norm_w, rows, g.K,
+                                       g.eps, s);
+            else
+                rmsnorm<__half>((__half *)norm_scratch, (const __half *)g.x, g.norm_w, rows, g.K, g.eps, s);
+            a.x = norm_scratch;
+            a.ldx = g.K;
+            ++n;
+        }
+        a.M = rows;
+        a.epi = g.epi;
+        a.out = g.out;
+        a.ldo = g.ldo;
+        a.bias = g.bias;
+        a.res = g.res;
+        a.ldr = g.ldr;
+        a.nq = g.nq;
+        a.nk = g.nk;
+        a.hd = g.hd;
+        a.freqs = g.freqs;
+        a.pos = g.pos;
+        a.seq = g.seq;
+        a.kpool = g.kpool;
+        a.vpool = g.vpool;
+        a.block_table = g.block_table;
+        a.max_pages = g.max_pages;
+        a.page = g.page;
+        a.kv_heads = g.kv_heads;
+        a.F = g.F;
+        a.err = g.err;
+        a.pdl = g.pdl;
+        gemm_tc(a, act, s);
+        return n + 1;
+    }
+    int n = 0;
+    for (int m0 = 0; m0 < rows; m0 += 8, ++n) {
+        GemvArgs a = g;
+        a.M = rows - m0 < 8 ? rows - m0 : 8;
+        a.x = (const char *)g.x + (size_t)m0 * g.ldx * es;
+        if (g.out && g.epi != EPI_LOGITS)
+            a.out = (char *)g.out + (size_t)m0 * g.ldo * (g.epi == EPI_PARTIAL ? 4 : es);
+        if (g.res) a.res = (const char *)g.res + (size_t)m0 * g.ldr * es;
+        if (g.pos) a.pos = g.pos + m0;
+        if (g.seq) a.seq = g.seq + m0;
+        if (g.tokens) a.tokens = g.tokens + m0;
+        if (g.best_val) {
+            a.best_val = g.best_val + m0;
+            a.best_key = g.best_key + m0;
+        }
+        if (m0) {
+            a.pf = nullptr;
+            a.pf_bytes = 0;
+        }
+        gemv(a, act, s);
+    }
+    return n;
+}
+
 }  // namespace wk
 
 using namespace wk;

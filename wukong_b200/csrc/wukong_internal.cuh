@@ -17,7 +17,8 @@ const CUtensorMap *weight_map(const void *w, long rows, long row_bytes, int box_
 void forget_weight_maps(const void *w);
 
 // ---------------------------------------------------------------- GEMV (gemv.cu)
-enum Epi : int { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4 };
+// PARTIAL: fp32 partial sums (no rounding) of a K-slice, reduced across ranks later.
+enum Epi : int { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4, EPI_PARTIAL = 5 };
 constexpr int kMaxLogitCtas = 512;
 
 struct GemvArgs {
@@ -52,6 +53,10 @@ struct GemvArgs {
     int *counter = nullptr;
     int *tokens = nullptr;
     int pack = 8;
+    long col_off = 0;   // vocabulary shard: global column of local row 0
+    int n_total = 0;    // vocabulary size of the whole row (0: N)
+    float *best_val = nullptr;             // optional per-row winner (value, key) instead of / beside tokens
+    unsigned long long *best_key = nullptr;
     const void *pf = nullptr;  // weights of a later kernel to prefetch into L2
     long pf_bytes = 0;
     int *err = nullptr;
@@ -126,10 +131,31 @@ void attention_qkv_rows(T *out, const T *qkv, int B, int Tn, int NH, int kvNH, i
 // GEMV (M <= 8 per pass) or the generic kernel.
 void matmul(void *out, const void *x, const void *w, const void *bias, int M, int K, int N, int wtype, int act,
             cudaStream_t s);
+// One linear layer with a fused epilogue over `rows` activation rows described
+// by `g` (g.M is ignored).  rows >= kTcMinRows run on the tcgen05 GEMM (an
+// RMSNorm prologue becomes a separate pass into norm_scratch, [rows, K]);
+// fewer rows run as GEMV passes of <= 8 rows (pf only on the first pass).
+// Returns the number of kernel launches.
+int linear(const GemvArgs &g, int rows, int act, cudaStream_t s, void *norm_scratch);
 // Fill per-row metadata: seq[i] = i / n, pos[i] = pos0 + i % n.
 void fill_row_meta(int *seq, int *pos, int rows, int n, int pos0, cudaStream_t s);
 // Identity block table: bt[b][p] = b * pages + p.
 void fill_block_table(int *bt, int batch, int pages, cudaStream_t s);
+
+// ---------------------------------------------------------------- tp.cu
+// Tensor parallelism over NCCL (one process per GPU); inactive until wk_tp_init.
+bool tp_active();
+int tp_rank();
+int tp_world();
+// in-place fp32 sum over the ranks
+void tp_allreduce_f32(float *buf, size_t n, cudaStream_t s);
+// bytes of one rank's logits winners for B rows: keys [B] u64, then values [B] f32
+size_t tp_winner_chunk(int B);
+// all-gather every rank's winners (send: one chunk, recv: world chunks) and
+// write the token of the best one per row
+void tp_argmax_combine(int *tokens, const void *send, void *recv, int B, int pack, cudaStream_t s);
+// x = T(x + T(p)) over n elements
+template <typename T> void resid_from_partial(T *x, const float *p, long n, cudaStream_t s);
 
 // ---------------------------------------------------------------- engine.cu
 // Records the message returned by wk_last_error() and returns -1.
