@@ -36,8 +36,11 @@ def _cfg(layers):
     return c
 
 
-@pytest.mark.parametrize("wtype,B", [(wk.Q8_0, 1), (wk.Q8_0, 3), (wk.F16, 1)])
-def test_engine_prefill_decode_vs_oracle(dev, wtype, B):
+@pytest.mark.parametrize("wtype,B,mk", [(wk.Q8_0, 1, "1"), (wk.Q8_0, 3, "1"), (wk.Q8_0, 3, "0"), (wk.F16, 1, "1")])
+def test_engine_prefill_decode_vs_oracle(dev, wtype, B, mk, monkeypatch):
+    """Decode steps run as the persistent kernel (Q8_0 with WUKONG_MEGAKERNEL=1)
+    or as the graph of per-op kernels (F16 weights, or WUKONG_MEGAKERNEL=0)."""
+    monkeypatch.setenv("WUKONG_MEGAKERNEL", mk)
     cfg, ctx, n, steps = _cfg(2), 64, 12, 10
     w = make_weights(cfg, wtype, wtype, wk.F16, seed=5, ctx=ctx)
     dm = DeviceModel(w)
@@ -68,7 +71,8 @@ def test_engine_prefill_decode_vs_oracle(dev, wtype, B):
                 assert near_tie(logits[b], got[b], ref[b]), (s, b, got[b], ref[b])
                 ties += 1
     assert ties <= 1 + (B * steps) // 10
-    assert L.wk_model_step_launches(m) == 1 + cfg["L"] * 5 + ((B + 7) // 8) + 1
+    persistent = wtype == wk.Q8_0 and mk == "1"
+    assert L.wk_model_step_launches(m) == (1 if persistent else 1 + cfg["L"] * 5 + ((B + 7) // 8) + 1)
     L.wk_model_destroy(m)
     free(pids, ptok)
     dm.free()

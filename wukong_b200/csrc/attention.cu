@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
                                                              long q_rs, const int *__restrict__ seq_of_row,
                                                              const int *__restrict__ pos_of_row, KVPaged kv, int G,
                                                              int Lpad_max, float scale, int *err, const void *pf,
-                                                             long pf_bytes) {
+                                                             long pf_bytes, int early) {
     constexpr int kPageBytes = kAttnPage * D * 2;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *ring = smem;                                                      // [slots][64][D] T
@@ -235,9 +235,12 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     mbar_fence_init();
     __syncthreads();
     const int total = 2 * npages;
-    // pages strictly before the newest token's page are complete: fetch them now
+    // When every row is the newest token of its sequence (decode), the pages
+    // before its page were written by earlier launches: fetch them before the
+    // wait for the producing kernel.  Otherwise (several rows of a sequence in
+    // this call) that kernel may still be writing them.
     int issued = 0;
-    if (tid == 0) {
+    if (tid == 0 && early) {
         for (; issued < kAttnSlots && issued < npages - 1; ++issued) {
             mbar_expect_tx(bars + issued, kPageBytes);
             bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
@@ -337,6 +340,14 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     for (int p = 0; p < npages; ++p, ++consumed) {
         const int slot = consumed % kAttnSlots;
         if (!mbar_wait_bounded(bars + slot, (consumed / kAttnSlots) & 1, err, 3)) ok = false;
+        if (p == npages - 1 && L % kAttnPage) {
+            // rows past the sequence end hold stale cache bytes; their P is 0, but 0 * NaN is NaN
+            T *vw = reinterpret_cast<T *>(ring + slot * kPageBytes);
+            const int r0 = L - p * kAttnPage;
+            for (int i = tid; i < (kAttnPage - r0) * D; i += 128) vw[r0 * D + i] = from_float<T>(0.f);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+        }
         const T *vt = reinterpret_cast<const T *>(ring + slot * kPageBytes);
         if (ok) {
 #pragma unroll
@@ -382,7 +393,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
 template <typename T, int D>
 void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
                       int nrows, int max_len, const KVPaged &kv, int G, cudaStream_t s, bool pdl, const void *pf,
-                      long pf_bytes) {
+                      long pf_bytes, bool early) {
     const int Lpad = (max_len + kAttnPage - 1) / kAttnPage * kAttnPage;
     const size_t smem = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 64 * 4 + 8 * D * 2 +
                         (size_t)8 * Lpad * 2;
@@ -405,7 +416,7 @@ void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq
     cfg.numAttrs = (pdl && g_rt.pdl) ? 1 : 0;
     const float scale = 1.0f / sqrtf((float)D);
     WK_CHECK(cudaLaunchKernelEx(&cfg, kern, out, out_rs, q, q_rs, seq_of_row, pos_of_row, kv, G, Lpad, scale,
-                                g_rt.d_error, pf, pf_bytes));
+                                g_rt.d_error, pf, pf_bytes, early ? 1 : 0));
 }
 
 }  // namespace
@@ -413,7 +424,7 @@ void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq
 template <typename T>
 void attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
                      int nrows, int max_len, const PagedKV &c, int H, cudaStream_t s, bool pdl, const void *pf,
-                     long pf_bytes) {
+                     long pf_bytes, bool early) {
     KVPaged kv{c.k, c.v, c.block_table, c.max_pages, c.page, c.kv_heads, c.hd};
     const int G = H / c.kv_heads;
     if constexpr (sizeof(T) == 2) {
@@ -421,22 +432,22 @@ void attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_
             ((uintptr_t)c.v % 16) == 0) {
             if (c.hd == 64)
                 launch_decode_tc<T, 64>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows, max_len, kv, G, s, pdl,
-                                        pf, pf_bytes);
+                                        pf, pf_bytes, early);
             else
                 launch_decode_tc<T, 128>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows, max_len, kv, G, s, pdl,
-                                         pf, pf_bytes);
+                                         pf, pf_bytes, early);
             return;
         }
     }
     launch_rows<T>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, 1, nrows, max_len, kv, H, c.kv_heads, c.hd, s, pdl);
 }
 template void attention_paged<__half>(__half *, long, const __half *, long, const int *, const int *, int, int,
-                                      const PagedKV &, int, cudaStream_t, bool, const void *, long);
+                                      const PagedKV &, int, cudaStream_t, bool, const void *, long, bool);
 template void attention_paged<__nv_bfloat16>(__nv_bfloat16 *, long, const __nv_bfloat16 *, long, const int *,
                                              const int *, int, int, const PagedKV &, int, cudaStream_t, bool,
-                                             const void *, long);
+                                             const void *, long, bool);
 template void attention_paged<float>(float *, long, const float *, long, const int *, const int *, int, int,
-                                     const PagedKV &, int, cudaStream_t, bool, const void *, long);
+                                     const PagedKV &, int, cudaStream_t, bool, const void *, long, bool);
 
 // Causal attention straight from fused QKV rows [B, T, (NH + 2 kvNH) HS]
 // (the layout cuda_gq_sdpa takes); out [B, T, NH HS].

@@ -11,6 +11,7 @@
 // one drains.  The reference computes the same step by re-running the whole
 // sequence through cuda.h (llm/llama.go:117-154, llm/model.go:158).
 #include <stdarg.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "wukong_ext.h"
@@ -186,6 +187,15 @@ struct wk_model {
     cudaGraphExec_t graph = nullptr;
     int graph_batch = 0;
     int step_launches = 0;
+    // persistent decode kernel (megakernel.cu): -1 not decided, 0 off, 1 on
+    int mk_mode = -1;
+    MkArgs mk;
+    MkLayer *d_mk_layers = nullptr;
+    CUtensorMap *d_mk_maps = nullptr;
+    unsigned long long *d_mk_bar = nullptr;
+    unsigned long long mk_base = 0;
+    int mk_stages = 0;
+    size_t mk_smem = 0;
 };
 
 namespace {
@@ -288,10 +298,10 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
         }
         if (m->act == kF16)
             attention_paged<__half>((__half *)m->att, col, (const __half *)m->q, col, seq, pos, rows, max_len, kv,
-                                    c.n_heads, s, true);
+                                    c.n_heads, s, true, nullptr, 0, rows == batch);
         else
             attention_paged<__nv_bfloat16>((__nv_bfloat16 *)m->att, col, (const __nv_bfloat16 *)m->q, col, seq, pos,
-                                           rows, max_len, kv, c.n_heads, s, true);
+                                           rows, max_len, kv, c.n_heads, s, true, nullptr, 0, rows == batch);
         ++launches;
         {
             GemvArgs a;
@@ -395,6 +405,93 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
     return launches;
 }
 
+// Decide once per model whether decode steps run as the persistent kernel
+// (opt-in: WUKONG_MEGAKERNEL=1), and build its per-layer tables and weight
+// tensor maps.  Not for tensor-parallel shards or shapes it does not take
+// (Q8_0 linear and output weights, K multiples of 256, head_dim 64 / 128, at
+// most 8 query heads per KV head, a context whose scores fit in shared memory).
+void mk_setup(wk_model *m) {
+    m->mk_mode = 0;
+    const char *env = getenv("WUKONG_MEGAKERNEL");
+    if (!env || env[0] != '1') return;
+    const wk_config &c = m->cfg;
+    const int D = c.head_dim, W = (c.n_heads + 2 * c.n_kv_heads) * D;
+    if (m->tp || m->act != kF16 || c.wtype != kQ8_0 || c.out_wtype != kQ8_0) return;
+    if (c.d_model % 256 || (c.n_heads * D) % 256 || c.ffn % 256 || (D != 64 && D != 128)) return;
+    if (c.n_heads % c.n_kv_heads || c.n_heads / c.n_kv_heads > 8 || !m->kpool) return;
+    if (c.embd_wtype != kF32 && c.embd_wtype != kF16 && c.embd_wtype != kBF16 && c.embd_wtype != kQ8_0) return;
+    MkArgs a = {};
+    a.L = c.n_layers;
+    a.d = c.d_model;
+    a.H = c.n_heads;
+    a.Hk = c.n_kv_heads;
+    a.D = D;
+    a.F = c.ffn;
+    a.V = c.vocab;
+    a.B = 8;  // shared memory is sized for the largest batch
+    a.eps = c.eps;
+    a.max_pages = m->max_pages;
+    a.lpad = (m->max_ctx + kPage - 1) / kPage * kPage;
+    int S = 0;
+    size_t smem = 0;
+    for (int st = 5; st >= 2 && !smem; --st) {
+        smem = mk_smem_bytes(a, st);
+        S = st;
+    }
+    if (!smem) return;
+    // tensor maps: qkv, o, fc (8-row boxes: up and gate halves), down per layer, then logits
+    const int L = c.n_layers;
+    CUtensorMap *maps = (CUtensorMap *)aligned_alloc(64, sizeof(CUtensorMap) * (4 * L + 1));
+    MkLayer *layers = (MkLayer *)calloc(L, sizeof(MkLayer));
+    bool ok = maps && layers;
+    auto enc = [&](CUtensorMap *mp, const void *w, long rows, int K, int box_rows) {
+        const long rb = (long)(K / 32) * 34;
+        ok = ok && ((uintptr_t)w % 16) == 0 &&
+             encode_map_2d(mp, w, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)rb / 2, (uint64_t)rows, (uint64_t)rb, 136,
+                           (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    };
+    for (int l = 0; ok && l < L; ++l) {
+        const Layer &Ly = m->layers[l];
+        enc(maps + 4 * l + 0, Ly.qkv, W, c.d_model, 16);
+        enc(maps + 4 * l + 1, Ly.o, c.d_model, c.n_heads * D, 16);
+        enc(maps + 4 * l + 2, Ly.fc, 2L * c.ffn, c.d_model, 8);
+        enc(maps + 4 * l + 3, Ly.down, c.d_model, c.ffn, 16);
+        layers[l] = MkLayer{Ly.qkv, Ly.o, Ly.fc, Ly.down, Ly.attn_norm, Ly.ffn_norm, m->kpool[l], m->vpool[l]};
+    }
+    if (ok) enc(maps + 4 * L, m->out_w, c.vocab, c.d_model, 16);
+    if (ok) ok = cudaMalloc(&m->d_mk_maps, sizeof(CUtensorMap) * (4 * L + 1)) == cudaSuccess &&
+                 cudaMalloc(&m->d_mk_layers, sizeof(MkLayer) * L) == cudaSuccess &&
+                 cudaMalloc(&m->d_mk_bar, sizeof(unsigned long long)) == cudaSuccess &&
+                 cudaMemcpy(m->d_mk_maps, maps, sizeof(CUtensorMap) * (4 * L + 1), cudaMemcpyHostToDevice) ==
+                     cudaSuccess &&
+                 cudaMemcpy(m->d_mk_layers, layers, sizeof(MkLayer) * L, cudaMemcpyHostToDevice) == cudaSuccess &&
+                 cudaMemset(m->d_mk_bar, 0, sizeof(unsigned long long)) == cudaSuccess;
+    free(maps);
+    free(layers);
+    if (!ok) {
+        cudaGetLastError();
+        return;
+    }
+    a.layers = m->d_mk_layers;
+    a.maps = m->d_mk_maps;
+    a.embd = m->embd;
+    a.embd_type = c.embd_wtype;
+    a.vocab_total = c.vocab;
+    a.out_norm = m->out_norm;
+    a.freqs = m->freqs;
+    a.block_table = m->block_table;
+    a.seq = m->d_seq;
+    a.part_val = m->part_val;
+    a.part_key = m->part_key;
+    a.bar = m->d_mk_bar;
+    a.err = g_rt.d_error;
+    m->mk = a;
+    m->mk_stages = S;
+    m->mk_smem = smem;
+    m->mk_base = 0;
+    m->mk_mode = 1;
+}
+
 void launch_embed(wk_model *m, const int *ids, int rows) {
     const wk_config &c = m->cfg;
     // the token table is whole on every rank; a shard's vocab counts only its logits rows
@@ -435,7 +532,7 @@ wk_model *wk_model_create(const wk_config *cfg) {
         fail("the engine needs F16 / BF16 / Q8_0 weights with 16/32-aligned widths");
         return nullptr;
     }
-    wk_model *m = (wk_model *)calloc(1, sizeof(wk_model));
+    wk_model *m = new wk_model();  // value-initialised: default member initialisers apply
     m->cfg = c;
     m->act = act;
     m->layers = (Layer *)calloc(c.n_layers, sizeof(Layer));
@@ -446,7 +543,7 @@ wk_model *wk_model_create(const wk_config *cfg) {
         cudaMemsetAsync(m->counter, 0, sizeof(int), s) != cudaSuccess) {
         fail("allocation failed");
         free(m->layers);
-        free(m);
+        delete m;
         return nullptr;
     }
     return m;
@@ -466,11 +563,11 @@ void wk_model_destroy(wk_model *m) {
     free(m->vpool);
     void *bufs[] = {m->block_table, m->d_pos, m->d_seq, m->d_ids, m->d_tokens, m->d_row_seq, m->d_row_pos,
                     m->x, m->q, m->att, m->h, m->xn, m->part_val, m->part_key, m->counter,
-                    m->p32, m->win_send, m->win_recv};
+                    m->p32, m->win_send, m->win_recv, m->d_mk_layers, m->d_mk_maps, m->d_mk_bar};
     for (void *p : bufs)
         if (p) cudaFree(p);
     free(m->layers);
-    free(m);
+    delete m;
 }
 
 int wk_model_set_layer(wk_model *m, int l, const void *attn_norm, const void *qkv, const void *o,
@@ -563,6 +660,32 @@ int wk_model_decode_step(wk_model *m) {
     set_device_current();
     cudaStream_t s = stream();
     const int B = m->batch;
+    if (m->mk_mode < 0) mk_setup(m);
+    if (m->mk_mode == 1 && B <= 8) {
+        if (ensure_rows(m, 8 * B)) return -1;
+        MkArgs a = m->mk;
+        a.B = B;
+        a.bar_base = m->mk_base;
+        a.ids = m->d_ids;
+        a.pos = m->d_pos;
+        a.tokens = m->d_tokens;
+        a.x = (__half *)m->x;
+        a.q = (__half *)m->q;
+        a.att = (__half *)m->att;
+        a.h = (__half *)m->h;
+        const cudaError_t e = mk_launch(a, m->mk_stages, m->mk_smem, s);
+        if (e == cudaSuccess) {
+            m->mk_base += (unsigned long long)mk_barriers(m->cfg.n_layers) * g_rt.num_sms;
+            m->step_launches = 1;
+            m->pos += 1;
+            return 0;
+        }
+        // the device cannot co-schedule it: use the graph path from now on
+        cudaGetLastError();
+        fprintf(stderr, "wukong: persistent decode kernel not launched (%s); using the per-op graph\n",
+                cudaGetErrorString(e));
+        m->mk_mode = 0;
+    }
     if (!m->graph) {
         if (ensure_rows(m, 8 * B)) return -1;
         WK_TRY(cudaStreamSynchronize(s));

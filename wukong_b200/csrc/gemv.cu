@@ -123,16 +123,18 @@ __device__ __forceinline__ void issue_unit(const GemvArgs &a, const Smem &sm, in
     }
 }
 
-// Issue the next unit of this warp's sequence into `slot`.
+// Issue the next unit of this warp's sequence into `slot` and advance the
+// cursor: chunks cstart, cstart + cstep, ... of tiles p_tile, p_tile + tstep, ...
 template <int WT>
 __device__ __forceinline__ void produce_unit(const GemvArgs &a, const Smem &sm, int w, int slot, int lane,
-                                             bool has_work, int ntiles, int nchunks, int &p_tile, int &p_chunk) {
+                                             bool has_work, int ntiles, int nchunks, int &p_tile, int &p_chunk,
+                                             int cstart, int cstep, int tstep) {
     if (has_work && p_tile < ntiles) {
         issue_unit<WT>(a, sm, w, slot, p_tile, p_chunk, lane, true);
-        p_chunk += kWarps;
+        p_chunk += cstep;
         if (p_chunk >= nchunks) {
-            p_chunk = w;
-            p_tile += gridDim.x;
+            p_chunk = cstart;
+            p_tile += tstep;
         }
     }
 }
@@ -321,6 +323,44 @@ __device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float &bes
     }
 }
 
+// Epilogue of a tile owned by one warp (SwiGLU or logits): lane (g, t) has
+// rows g, g + 8 for columns 2t, 2t + 1 (SwiGLU: up row g, gate row g + 8).
+template <typename T>
+__device__ __forceinline__ void warp_epilogue(const GemvArgs &a, int tile, int g, int t, const float (&c)[2][4],
+                                              float (&bv)[2], uint64_t (&bk)[2]) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int m = 2 * t + j;
+        const float lo = c[0][j] + c[1][j], hi = c[0][2 + j] + c[1][2 + j];
+        if (m >= a.M) continue;
+        if (a.epi == EPI_SWIGLU) {
+            if (tile * 8 + g < a.F) {
+                const float u = round_to<T>(lo);
+                const float gt = round_to<T>(hi);
+                const float sig = 1.0f / (1.0f + expf(-gt));
+                reinterpret_cast<T *>(a.out)[(long)m * a.ldo + tile * 8 + g] = from_float<T>((gt * sig) * u);
+            }
+        } else {  // EPI_LOGITS
+            const long lim = (long)((a.n_total ? a.n_total : a.N) / a.pack) * a.pack;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int n = tile * kTileRows + g + 8 * h;
+                if (n >= a.N) continue;
+                const float y = round_to<T>(h ? hi : lo);
+                if (a.out) reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(y);
+                const long gn = (long)n + a.col_off;
+                if (gn < lim && (y > bv[j] || (y == bv[j] && bk[j] != ~0ull))) {
+                    const uint64_t k = logits_key(gn, a.pack);
+                    if (y > bv[j] || k < bk[j]) {
+                        bv[j] = y;
+                        bk[j] = k;
+                    }
+                }
+            }
+        }
+    }
+}
+
 template <typename T, int WT>
 __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
     using F = WFmt<WT>;
@@ -351,11 +391,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     __syncthreads();
     if (threadIdx.x == 32 && a.pf) l2_prefetch_slice(a.pf, a.pf_bytes, blockIdx.x, gridDim.x);
 
-    // this warp's unit sequence: tiles blockIdx.x, +gridDim.x, ...; chunks w, w+8, ...
-    int p_tile = blockIdx.x, p_chunk = w;  // producer cursor
-    const bool has_work = w < nchunks;     // a warp with no chunk in this K idles in the k-loop
+    // this warp's unit sequence.  CTA tiles: tiles blockIdx.x, +gridDim.x, ...,
+    // chunks w, w + 8, ...; warp tiles: tiles gw, gw + 8 gridDim.x, ..., all chunks
+    const bool wmode = warp_tiles(a.epi, ntiles);
+    const int gw = blockIdx.x * kWarps + w, nw = gridDim.x * kWarps;
+    const int cstart = wmode ? 0 : w, cstep = wmode ? 1 : kWarps, tstep = wmode ? nw : (int)gridDim.x;
+    int p_tile = wmode ? gw : (int)blockIdx.x, p_chunk = cstart;  // producer cursor
+    const bool has_work = wmode || w < nchunks;  // a warp with no chunk in this K idles in the k-loop
     if (tma)
-        for (int s = 0; s < kStages; ++s) produce_unit<WT>(a, sm, w, s, lane, has_work, ntiles, nchunks, p_tile, p_chunk);
+        for (int s = 0; s < kStages; ++s)
+            produce_unit<WT>(a, sm, w, s, lane, has_work, ntiles, nchunks, p_tile, p_chunk, cstart, cstep, tstep);
     // weights are in flight; wait for the producer of X, then let the next kernel
     // in the stream start its own weight prefetch
     pdl_wait();
@@ -367,7 +412,56 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     uint64_t best_k = ~0ull;
     int consumed = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    if (wmode) {
+        // lane (g, t) holds rows g, g + 8 and columns 2t, 2t + 1 of each of its tiles
+        const int g = lane >> 2, t = lane & 3;
+        float bv[2] = {-INFINITY, -INFINITY};
+        uint64_t bk[2] = {~0ull, ~0ull};
+        for (int tile = gw; tile < ntiles; tile += nw) {
+            float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            for (int chunk = 0; chunk < nchunks; ++chunk) {
+                const int slot = consumed % kStages;
+                if (tma) {
+                    if (!mbar_wait_bounded(sm.bars + w * kStages + slot, (consumed / kStages) & 1, a.err, 1))
+                        ok = false;
+                } else {
+                    issue_unit<WT>(a, sm, w, slot, tile, chunk, lane, false);
+                    __syncwarp();
+                }
+                if (ok) consume_unit<WT>(a, sm, w, slot, chunk, lane, c);
+                __syncwarp();
+                ++consumed;
+                if (tma && ok)
+                    produce_unit<WT>(a, sm, w, slot, lane, has_work, ntiles, nchunks, p_tile, p_chunk, cstart, cstep,
+                                     tstep);
+            }
+            warp_epilogue<T>(a, tile, g, t, c, bv, bk);
+        }
+        if (a.epi == EPI_LOGITS) {
+            // best of the 8 lanes that share t, then one (value, key) per warp and column
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv[j], o);
+                    const uint64_t okey = __shfl_xor_sync(0xffffffffu, bk[j], o);
+                    if (ov > bv[j] || (ov == bv[j] && okey < bk[j])) {
+                        bv[j] = ov;
+                        bk[j] = okey;
+                    }
+                }
+            float *sv = sm.misc + 8;
+            uint64_t *sk = reinterpret_cast<uint64_t *>(sm.misc + 8 + 128);
+            if (g == 0) {
+                sv[w * 8 + 2 * t] = bv[0];
+                sk[w * 8 + 2 * t] = bk[0];
+                sv[w * 8 + 2 * t + 1] = bv[1];
+                sk[w * 8 + 2 * t + 1] = bk[1];
+            }
+        }
+        __syncthreads();
+    }
+    for (int tile = blockIdx.x; !wmode && tile < ntiles; tile += gridDim.x) {
         float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         if (has_work) {
             for (int chunk = w; chunk < nchunks; chunk += kWarps) {
@@ -383,7 +477,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
                 if (ok) consume_unit<WT>(a, sm, w, slot, chunk, lane, c);
                 __syncwarp();  // the slot is free again
                 ++consumed;
-                if (tma && ok) produce_unit<WT>(a, sm, w, slot, lane, has_work, ntiles, nchunks, p_tile, p_chunk);
+                if (tma && ok)
+                    produce_unit<WT>(a, sm, w, slot, lane, has_work, ntiles, nchunks, p_tile, p_chunk, cstart, cstep,
+                                     tstep);
             }
         }
         // partial tile of this warp -> shared memory (rows g, g+8; columns 2t, 2t+1)
@@ -401,9 +497,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     if (a.epi == EPI_LOGITS) {
         // per-CTA argmax partials: reduce over the 16 row-threads of each column m
         const int tid = threadIdx.x, m = tid & 7;
-        float *sv = sm.misc + 8;                                        // [16][8]
-        uint64_t *sk = reinterpret_cast<uint64_t *>(sm.misc + 8 + 128);  // [16][8]
-        if (tid < 128) {
+        float *sv = sm.misc + 8;                                        // [16][8] or [8 warps][8]
+        uint64_t *sk = reinterpret_cast<uint64_t *>(sm.misc + 8 + 128);  // (written above in warp mode)
+        if (!wmode && tid < 128) {
             sv[tid] = best_v;
             sk[tid] = best_k;
         }
@@ -411,7 +507,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         if (tid < 8 && tid < a.M) {
             float v = sv[tid];
             uint64_t k = sk[tid];
-            for (int r = 1; r < 16; ++r) {
+            for (int r = 1; r < (wmode ? kWarps : 16); ++r) {
                 const float ov = sv[r * 8 + tid];
                 const uint64_t ok = sk[r * 8 + tid];
                 if (ov > v || (ov == v && ok < k)) {

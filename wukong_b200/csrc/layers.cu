@@ -258,10 +258,11 @@ void gqa_fused(void *out, const void *embeds, const float *freqs, const float *n
         linear(a, rows, act, stream(), xn);
     }
     if (act == kF16)
-        attention_paged<__half>((__half *)att, col, (const __half *)q, col, seq, pos, rows, row, kv, NH, stream(), true);
+        attention_paged<__half>((__half *)att, col, (const __half *)q, col, seq, pos, rows, row, kv, NH, stream(), true,
+                                nullptr, 0, r.n == 1);
     else
         attention_paged<__nv_bfloat16>((__nv_bfloat16 *)att, col, (const __nv_bfloat16 *)q, col, seq, pos, rows, row,
-                                       kv, NH, stream(), true);
+                                       kv, NH, stream(), true, nullptr, 0, r.n == 1);
     {
         GemvArgs a;
         a.w = (const uint8_t *)out_w;

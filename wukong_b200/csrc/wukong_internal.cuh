@@ -66,6 +66,16 @@ struct GemvArgs {
 static_assert(alignof(GemvArgs) >= 64, "the tensor map must stay 64-byte aligned");
 
 bool gemv_supported(int wtype, int act, int K);
+// Linear layers with many 16-row tiles (the SwiGLU up|gate layer and the logits
+// of Llama-sized models) give each warp whole tiles: all K-chunks accumulate in
+// one warp, in K order, and the warp applies the epilogue itself.  Fewer tiles
+// are split over the 8 warps of a CTA by K-chunk and reduced in shared memory.
+// The rule depends only on the layer shape, so the per-op GEMV and the
+// persistent decode kernel round identically.
+constexpr int kWarpTileMin = 1024;
+__host__ __device__ inline bool warp_tiles(int epi, int ntiles) {
+    return (epi == EPI_SWIGLU || epi == EPI_LOGITS) && ntiles >= kWarpTileMin;
+}
 void gemv(GemvArgs a, int act, cudaStream_t s);
 
 // ---------------------------------------------------------------- tcgen05 GEMM (gemm_tc.cu)
@@ -119,10 +129,13 @@ struct PagedKV {
     const int *block_table = nullptr;  // [seqs][max_pages]
     int max_pages = 0, page = 0, kv_heads = 0, hd = 0;
 };
+// early: every row is the newest token of its sequence and older pages were
+// written by earlier launches (decode), so they may be fetched before the
+// programmatic-dependent-launch wait.
 template <typename T>
 void attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
                      int nrows, int max_len, const PagedKV &c, int H, cudaStream_t s, bool pdl,
-                     const void *pf = nullptr, long pf_bytes = 0);
+                     const void *pf = nullptr, long pf_bytes = 0, bool early = false);
 template <typename T>
 void attention_qkv_rows(T *out, const T *qkv, int B, int Tn, int NH, int kvNH, int HS, cudaStream_t s);
 
@@ -141,6 +154,39 @@ int linear(const GemvArgs &g, int rows, int act, cudaStream_t s, void *norm_scra
 void fill_row_meta(int *seq, int *pos, int rows, int n, int pos0, cudaStream_t s);
 // Identity block table: bt[b][p] = b * pages + p.
 void fill_block_table(int *bt, int batch, int pages, cudaStream_t s);
+
+// ---------------------------------------------------------------- megakernel.cu
+// One decode step of the engine as a single persistent cooperative kernel
+// (batch <= 8, Q8_0 weights, fp16 activations).
+struct MkLayer {
+    const uint8_t *qkv, *o, *fc, *down;
+    const float *attn_norm, *ffn_norm;
+    void *kpool, *vpool;
+};
+struct MkArgs {
+    int L, d, H, Hk, D, F, V, B;
+    float eps;
+    int max_pages, lpad;            // KV block-table width; score row length (>= context, multiple of 64)
+    const MkLayer *layers;          // device [L]
+    const CUtensorMap *maps;        // device [4 L + 1]: per layer qkv, o, fc (8-row boxes), down; then logits
+    const uint8_t *embd;
+    int embd_type, vocab_total;
+    const float *out_norm, *freqs;
+    const int *block_table, *seq;
+    int *ids, *pos, *tokens;        // [B]: inputs, positions (advanced by the kernel), outputs
+    __half *x, *q, *att, *h;        // activations [B][d], [B][H D], [B][H D], [B][F]
+    float *part_val;                // [grid][8] logits winners per CTA
+    unsigned long long *part_key;
+    unsigned long long *bar;        // grid barrier counter (monotonic across launches)
+    unsigned long long bar_base;    // its value when this launch starts
+    int *err;
+};
+// Grid barriers per launch (arrivals per CTA).
+inline int mk_barriers(int L) { return 5 * L + 2; }
+// Shared memory of the kernel for `stages` weight units in flight per warp (0 if it does not fit).
+size_t mk_smem_bytes(const MkArgs &a, int stages);
+// Cooperative launch on every SM; an error (nothing launched) when the device cannot co-schedule it.
+cudaError_t mk_launch(const MkArgs &a, int stages, size_t smem, cudaStream_t s);
 
 // ---------------------------------------------------------------- tp.cu
 // Tensor parallelism over NCCL (one process per GPU); inactive until wk_tp_init.
