@@ -22,6 +22,8 @@ pytestmark = pytest.mark.gpu
 
 def _decode(monkeypatch, mk, dm, w, cfg, B, ctx, ids, steps):
     monkeypatch.setenv("WUKONG_MEGAKERNEL", mk)
+    # the persistent kernel runs one CTA per (row, kv head); so does the reference path here
+    monkeypatch.setenv("WUKONG_SPLIT_ATTN", "0")
     L = wk.lib()
     m = build_engine(dm, w, cfg, wk.Q8_0, wk.Q8_0, wk.F16, max_batch=B, ctx=ctx)
     pids, ptok = up(ids), alloc(4 * B)

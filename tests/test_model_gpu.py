@@ -78,6 +78,43 @@ def test_engine_prefill_decode_vs_oracle(dev, wtype, B, mk, monkeypatch):
     dm.free()
 
 
+@pytest.mark.parametrize("B", [1, 3])
+def test_engine_long_context_split_attention_vs_oracle(dev, B, monkeypatch):
+    """Decode at a 520..526-token context (9+ pages), where attention splits the
+    pages of each (sequence, kv head) over several CTAs (two launches);
+    teacher-forced against the oracle like the short-context test."""
+    monkeypatch.setenv("WUKONG_MEGAKERNEL", "0")
+    monkeypatch.delenv("WUKONG_SPLIT_ATTN", raising=False)
+    cfg, ctx, n, steps = _cfg(1), 640, 520, 6
+    w = make_weights(cfg, wk.Q8_0, wk.Q8_0, wk.F16, seed=11, ctx=ctx)
+    dm = DeviceModel(w)
+    m = build_engine(dm, w, cfg, wk.Q8_0, wk.Q8_0, wk.F16, max_batch=B, ctx=ctx)
+    om = oracle_model(w, cfg, wk.Q8_0, wk.Q8_0, wk.F16, ctx)
+    om.reset(B)
+    L = wk.lib()
+    ids = np.random.default_rng(5).integers(0, cfg["V"], size=(B, n)).astype(np.int32)
+    pids, ptok = up(ids), alloc(4 * B)
+    wk.check(L.wk_model_prefill(m, pids, B, n, ptok))
+    ref, logits, _ = om.forward(ids)
+    ties = 0
+    for s in range(steps):
+        nxt = L.wk_model_next_ids(m)
+        L.cuda_to_device(nxt, ref.ctypes.data_as(ctypes.c_void_p), 4 * B)
+        wk.check(L.wk_model_decode_step(m))
+        got = down(L.wk_model_tokens(m), B, np.int32)
+        ref, logits, _ = om.forward(ref.reshape(B, 1))
+        for b in range(B):
+            if got[b] != ref[b]:
+                assert near_tie(logits[b], got[b], ref[b]), (s, b, got[b], ref[b])
+                ties += 1
+    assert ties <= 1 + (B * steps) // 10
+    # 1 layer: embed, qkv, attention scores + pv, o, fc, down, logits, advance
+    assert L.wk_model_step_launches(m) == 1 + 6 + ((B + 7) // 8) + 1
+    L.wk_model_destroy(m)
+    free(pids, ptok)
+    dm.free()
+
+
 def test_host_mirror_generate_vs_oracle(dev):
     """model.go's loop (full re-prefill each step) through cuda.h, vs the oracle."""
     cfg, ctx = _cfg(2), 48

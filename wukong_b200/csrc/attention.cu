@@ -10,6 +10,8 @@
 // for keys j <= p.  This kernel computes exactly these rounding points in one
 // pass per (query row, KV head): the GQA group's query heads share the K/V
 // rows, which are read once per CTA (no replication, no permutes).
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "wukong_internal.cuh"
 
@@ -390,6 +392,309 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     }
 }
 
+// ---------------------------------------------------------------- split-K decode attention
+// For few (row, kv head) pairs and long contexts the pages are split over
+// gridDim.z CTAs in two launches with the reference's rounding points intact:
+//   scores:  s_j = T(q . k_j) of this split's keys -> global score rows, and the
+//            split's max of s_j * scale per head;
+//   pv:      every split CTA takes M = max over splits and the softmax sum over
+//            the whole row in the single-CTA kernel's order (same e_j, same sum,
+//            same P_j = T(T(e_j) / sum)), multiplies its own V pages, writes an
+//            fp32 partial, and the last CTA of the (row, head) adds the partials
+//            in split order and stores T(o).
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restrict__ q, long q_rs,
+                                                                const int *__restrict__ seq_of_row,
+                                                                const int *__restrict__ pos_of_row, KVPaged kv, int G,
+                                                                int pps, int lpad, float scale, T *__restrict__ S,
+                                                                float *__restrict__ mpart, int *err, int early) {
+    constexpr int kPageBytes = kAttnPage * D * 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *ring = smem;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnSlots * kPageBytes);
+    float *red = reinterpret_cast<float *>(bars + kAttnSlots);  // [8][4]
+    T *qs = reinterpret_cast<T *>(red + 32);                     // [8][D]
+    const int kvh = blockIdx.x, row = blockIdx.y, z = blockIdx.z, nz = gridDim.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int seq = seq_of_row[row], pos = pos_of_row[row];
+    const int L = pos + 1;
+    const int npages = (L + kAttnPage - 1) / kAttnPage;
+    const int p0 = z * pps, p1 = min(p0 + pps, npages);
+    const int n = p1 > p0 ? p1 - p0 : 0;
+    const T *K = reinterpret_cast<const T *>(kv.k);
+    auto page_src = [&](int i) -> const T * {
+        const long pg = kv.block_table[(long)seq * kv.max_pages + p0 + i];
+        return K + (pg * kv.kv_heads + kvh) * (long)kAttnPage * D;
+    };
+    if (tid < kAttnSlots) mbar_init(bars + tid, 1);
+    mbar_fence_init();
+    __syncthreads();
+    int issued = 0;
+    if (tid == 0 && early)  // decode: pages before the newest one were written by earlier launches
+        for (; issued < kAttnSlots && issued < n && p0 + issued < npages - 1; ++issued) {
+            mbar_expect_tx(bars + issued, kPageBytes);
+            bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
+        }
+    pdl_wait();
+    pdl_trigger();
+    if (tid == 0)
+        for (; issued < kAttnSlots && issued < n; ++issued) {
+            mbar_expect_tx(bars + issued, kPageBytes);
+            bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
+        }
+    const T *qrow = q + (long)row * q_rs + (long)kvh * G * D;
+    for (int i = tid; i < 8 * D; i += 128) qs[i] = i < G * D ? qrow[i] : from_float<T>(0.f);
+    __syncthreads();
+    uint32_t qb[D / 16][2];
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+        qb[kk][0] = *reinterpret_cast<const uint32_t *>(qs + g * D + kk * 16 + 2 * t);
+        qb[kk][1] = *reinterpret_cast<const uint32_t *>(qs + g * D + kk * 16 + 2 * t + 8);
+    }
+    T *srow = S + ((long)row * kv.kv_heads + kvh) * 8 * lpad;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+        const int slot = i % kAttnSlots;
+        if (!mbar_wait_bounded(bars + slot, (i / kAttnSlots) & 1, err, 4)) ok = false;
+        const T *kt = reinterpret_cast<const T *>(ring + slot * kPageBytes) + warp * 16 * D;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ok) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(smem_u32(kt + (lane & 15) * D + kk * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
+                mma16<T>(c, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+            }
+        }
+        const int k0 = (p0 + i) * kAttnPage + warp * 16 + g;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int key = k0 + (j >> 1) * 8, h = 2 * t + (j & 1);
+            const float sv = key < L ? round_to<T>(c[j]) : -INFINITY;
+            srow[(long)h * lpad + key] = from_float<T>(key < L ? sv : 0.f);
+            if (j & 1)
+                mx1 = fmaxf(mx1, sv * scale);
+            else
+                mx0 = fmaxf(mx0, sv * scale);
+        }
+        __syncthreads();
+        if (tid == 0 && issued < n) {
+            const int sl = issued % kAttnSlots;
+            mbar_expect_tx(bars + sl, kPageBytes);
+            bulk_g2s(ring + sl * kPageBytes, page_src(issued), kPageBytes, bars + sl);
+            ++issued;
+        }
+    }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    if (g == 0) {
+        red[(2 * t) * 4 + warp] = mx0;
+        red[(2 * t + 1) * 4 + warp] = mx1;
+    }
+    __syncthreads();
+    if (tid < 8)
+        mpart[(((long)row * kv.kv_heads + kvh) * nz + z) * 8 + tid] =
+            fmaxf(fmaxf(red[tid * 4], red[tid * 4 + 1]), fmaxf(red[tid * 4 + 2], red[tid * 4 + 3]));
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out, long out_rs,
+                                                            const int *__restrict__ seq_of_row,
+                                                            const int *__restrict__ pos_of_row, KVPaged kv, int G,
+                                                            int pps, int lpad, float scale, const T *__restrict__ S,
+                                                            const float *__restrict__ mpart, float *__restrict__ opart,
+                                                            int *__restrict__ counter, int *err, int early) {
+    constexpr int kPageBytes = kAttnPage * D * 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *ring = smem;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnSlots * kPageBytes);
+    float *Ms = reinterpret_cast<float *>(bars + kAttnSlots);  // [8]
+    T *pl = reinterpret_cast<T *>(Ms + 8);                     // [8][pps * 64] this split's P
+    __shared__ int last;
+    const int kvh = blockIdx.x, row = blockIdx.y, z = blockIdx.z, nz = gridDim.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int seq = seq_of_row[row], pos = pos_of_row[row];
+    const int L = pos + 1;
+    const int npages = (L + kAttnPage - 1) / kAttnPage;
+    const int Lpad = npages * kAttnPage;
+    const int p0 = z * pps, p1 = min(p0 + pps, npages);
+    const int n = p1 > p0 ? p1 - p0 : 0;
+    const int wl = pps * kAttnPage;  // row length of pl
+    const T *V = reinterpret_cast<const T *>(kv.v);
+    auto page_src = [&](int i) -> const T * {
+        const long pg = kv.block_table[(long)seq * kv.max_pages + p0 + i];
+        return V + (pg * kv.kv_heads + kvh) * (long)kAttnPage * D;
+    };
+    if (tid < kAttnSlots) mbar_init(bars + tid, 1);
+    mbar_fence_init();
+    __syncthreads();
+    int issued = 0;
+    if (tid == 0 && early)
+        for (; issued < kAttnSlots && issued < n && p0 + issued < npages - 1; ++issued) {
+            mbar_expect_tx(bars + issued, kPageBytes);
+            bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
+        }
+    pdl_wait();
+    pdl_trigger();
+    if (tid == 0)
+        for (; issued < kAttnSlots && issued < n; ++issued) {
+            mbar_expect_tx(bars + issued, kPageBytes);
+            bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
+        }
+    const long rh = (long)row * kv.kv_heads + kvh;
+    if (tid < 8) {
+        float m = -INFINITY;
+        for (int zz = 0; zz < nz; ++zz) m = fmaxf(m, mpart[(rh * nz + zz) * 8 + tid]);
+        Ms[tid] = m;
+    }
+    __syncthreads();
+    // softmax over the whole row, in the single-CTA kernel's order
+    {
+        const int h = tid >> 4, i0 = tid & 15;
+        const T *sr = S + (rh * 8 + h) * lpad;
+        const float M = Ms[h];
+        float lsum = 0.f;
+        for (int j = i0; j < Lpad; j += 16)
+            if (j < L && h < G) lsum += expf(to_float(sr[j]) * scale - M);
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+        const float inv = 1.0f / lsum;
+        for (int jj = i0; jj < n * kAttnPage; jj += 16) {
+            const int j = p0 * kAttnPage + jj;
+            float pv = 0.f;
+            if (j < L && h < G) pv = to_float(from_float<T>(to_float(from_float<T>(expf(to_float(sr[j]) * scale - M))) * inv));
+            pl[h * wl + jj] = from_float<T>(pv);
+        }
+    }
+    __syncthreads();
+    constexpr int kDT = D / 16;
+    constexpr int kNA = kDT > 4 ? 2 : 1;
+    float o[kNA][4];
+#pragma unroll
+    for (int a = 0; a < kNA; ++a) o[a][0] = o[a][1] = o[a][2] = o[a][3] = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+        const int slot = i % kAttnSlots;
+        if (!mbar_wait_bounded(bars + slot, (i / kAttnSlots) & 1, err, 5)) ok = false;
+        if (p0 + i == npages - 1 && L % kAttnPage) {
+            // rows past the sequence end hold stale cache bytes; their P is 0, but 0 * NaN is NaN
+            T *vw = reinterpret_cast<T *>(ring + slot * kPageBytes);
+            const int r0 = L - (p0 + i) * kAttnPage;
+            for (int e = tid; e < (kAttnPage - r0) * D; e += 128) vw[r0 * D + e] = from_float<T>(0.f);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+        }
+        const T *vt = reinterpret_cast<const T *>(ring + slot * kPageBytes);
+        if (ok) {
+#pragma unroll
+            for (int ks = 0; ks < kAttnPage / 16; ++ks) {
+                const int key0 = i * kAttnPage + ks * 16;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(pl + g * wl + key0 + 2 * t);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(pl + g * wl + key0 + 2 * t + 8);
+#pragma unroll
+                for (int a = 0; a < kNA; ++a) {
+                    const int d0 = (warp + 4 * a) * 16;
+                    const int mi = lane >> 3, r = lane & 7;
+                    const T *addr = vt + (ks * 16 + r + (mi >> 1) * 8) * D + d0 + (mi & 1) * 8;
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(smem_u32(addr), a0, a1, a2, a3);
+                    mma16<T>(o[a], a0, a1, a2, a3, b0, b1);
+                }
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && issued < n) {
+            const int sl = issued % kAttnSlots;
+            mbar_expect_tx(bars + sl, kPageBytes);
+            bulk_g2s(ring + sl * kPageBytes, page_src(issued), kPageBytes, bars + sl);
+            ++issued;
+        }
+    }
+    // partial O^T of this split: rows d, columns (heads) 2t, 2t + 1
+    float *op = opart + (rh * nz + z) * 8 * D;
+#pragma unroll
+    for (int a = 0; a < kNA; ++a) {
+        const int d0 = (warp + 4 * a) * 16;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int d = d0 + g + (i >> 1) * 8, hh = 2 * t + (i & 1);
+            op[hh * D + d] = o[a][i];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(counter + rh, 1) == nz - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    T *orow = out + (long)row * out_rs + (long)kvh * G * D;
+    for (int i = tid; i < G * D; i += 128) {
+        float acc = 0.f;
+        for (int zz = 0; zz < nz; ++zz) acc += __ldcg(opart + (rh * nz + zz) * 8 * D + i);
+        orow[i] = from_float<T>(acc);
+    }
+    if (tid == 0) counter[rh] = 0;
+}
+
+template <typename T, int D>
+bool launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
+                  int nrows, int max_len, const KVPaged &kv, int G, cudaStream_t s, bool pdl, bool early,
+                  const AttnSplitWs &ws) {
+    const char *env = getenv("WUKONG_SPLIT_ATTN");  // 0: one CTA per (row, kv head) always
+    if (env && env[0] == '0') return false;
+    const int pages = (max_len + kAttnPage - 1) / kAttnPage;
+    const int units = nrows * kv.kv_heads;
+    int nz = (2 * g_rt.num_sms + units - 1) / units;
+    if (nz > pages) nz = pages;
+    if (nz > ws.max_splits) nz = ws.max_splits;
+    // below 8 pages the second launch costs more than the split saves
+    if (pages < 8 || nz < 2 || nrows > ws.max_rows || pages * kAttnPage > ws.lpad || kv.kv_heads > ws.max_kv_heads)
+        return false;
+    const int pps = (pages + nz - 1) / nz;
+    nz = (pages + pps - 1) / pps;
+    if (nz < 2) return false;
+    const float scale = 1.0f / sqrtf((float)D);
+    const size_t smem_a = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 32 * 4 + 8 * D * 2;
+    const size_t smem_b = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 8 * 4 + (size_t)8 * pps * kAttnPage * 2;
+    if ((int)smem_b > g_rt.max_smem_optin) return false;
+    auto ka = attn_split_scores_kernel<T, D>;
+    auto kb = attn_split_pv_kernel<T, D>;
+    static int conf_a = 0, conf_b = 0;
+    if ((int)smem_a > conf_a) {
+        WK_CHECK(cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_a));
+        conf_a = (int)smem_a;
+    }
+    if ((int)smem_b > conf_b) {
+        WK_CHECK(cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b));
+        conf_b = (int)smem_b;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kv.kv_heads, nrows, nz);
+    cfg.blockDim = dim3(128);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (pdl && g_rt.pdl) ? 1 : 0;
+    cfg.dynamicSmemBytes = smem_a;
+    WK_CHECK(cudaLaunchKernelEx(&cfg, ka, q, q_rs, seq_of_row, pos_of_row, kv, G, pps, ws.lpad, scale,
+                                (T *)ws.scores, ws.mpart, g_rt.d_error, early ? 1 : 0));
+    cfg.dynamicSmemBytes = smem_b;
+    cfg.numAttrs = g_rt.pdl ? 1 : 0;
+    WK_CHECK(cudaLaunchKernelEx(&cfg, kb, out, out_rs, seq_of_row, pos_of_row, kv, G, pps, ws.lpad, scale,
+                                (const T *)ws.scores, (const float *)ws.mpart, ws.opart, ws.counter, g_rt.d_error,
+                                early ? 1 : 0));
+    return true;
+}
+
 template <typename T, int D>
 void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
                       int nrows, int max_len, const KVPaged &kv, int G, cudaStream_t s, bool pdl, const void *pf,
@@ -422,32 +727,40 @@ void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq
 }  // namespace
 
 template <typename T>
-void attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
+int attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
                      int nrows, int max_len, const PagedKV &c, int H, cudaStream_t s, bool pdl, const void *pf,
-                     long pf_bytes, bool early) {
+                     long pf_bytes, bool early, const AttnSplitWs *ws) {
     KVPaged kv{c.k, c.v, c.block_table, c.max_pages, c.page, c.kv_heads, c.hd};
     const int G = H / c.kv_heads;
     if constexpr (sizeof(T) == 2) {
         if (c.page == kAttnPage && G <= 8 && (c.hd == 64 || c.hd == 128) && ((uintptr_t)c.k % 16) == 0 &&
             ((uintptr_t)c.v % 16) == 0) {
+            if (ws && (c.hd == 64 ? launch_split<T, 64>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows, max_len,
+                                                        kv, G, s, pdl, early, *ws)
+                                  : launch_split<T, 128>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows,
+                                                         max_len, kv, G, s, pdl, early, *ws)))
+                return 2;
             if (c.hd == 64)
                 launch_decode_tc<T, 64>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows, max_len, kv, G, s, pdl,
                                         pf, pf_bytes, early);
             else
                 launch_decode_tc<T, 128>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows, max_len, kv, G, s, pdl,
                                          pf, pf_bytes, early);
-            return;
+            return 1;
         }
     }
     launch_rows<T>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, 1, nrows, max_len, kv, H, c.kv_heads, c.hd, s, pdl);
+    return 1;
 }
-template void attention_paged<__half>(__half *, long, const __half *, long, const int *, const int *, int, int,
-                                      const PagedKV &, int, cudaStream_t, bool, const void *, long, bool);
-template void attention_paged<__nv_bfloat16>(__nv_bfloat16 *, long, const __nv_bfloat16 *, long, const int *,
+template int attention_paged<__half>(__half *, long, const __half *, long, const int *, const int *, int, int,
+                                      const PagedKV &, int, cudaStream_t, bool, const void *, long, bool,
+                                      const AttnSplitWs *);
+template int attention_paged<__nv_bfloat16>(__nv_bfloat16 *, long, const __nv_bfloat16 *, long, const int *,
                                              const int *, int, int, const PagedKV &, int, cudaStream_t, bool,
-                                             const void *, long, bool);
-template void attention_paged<float>(float *, long, const float *, long, const int *, const int *, int, int,
-                                     const PagedKV &, int, cudaStream_t, bool, const void *, long, bool);
+                                             const void *, long, bool, const AttnSplitWs *);
+template int attention_paged<float>(float *, long, const float *, long, const int *, const int *, int, int,
+                                     const PagedKV &, int, cudaStream_t, bool, const void *, long, bool,
+                                     const AttnSplitWs *);
 
 // Causal attention straight from fused QKV rows [B, T, (NH + 2 kvNH) HS]
 // (the layout cuda_gq_sdpa takes); out [B, T, NH HS].

@@ -180,6 +180,7 @@ struct wk_model {
     int tp = 0;
     float *p32 = nullptr;                           // [rows_cap, d] fp32 partials of o / down
     void *win_send = nullptr, *win_recv = nullptr;  // logits winners of this rank / of all ranks
+    AttnSplitWs attn_ws;                             // split-K decode attention scratch
     // logits argmax partials
     float *part_val = nullptr;
     unsigned long long *part_key = nullptr;
@@ -296,13 +297,17 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.pf_bytes = wbytes(d, col, c.wtype);
             launches += linear(a, rows, m->act, s, m->xn);
         }
-        if (m->act == kF16)
-            attention_paged<__half>((__half *)m->att, col, (const __half *)m->q, col, seq, pos, rows, max_len, kv,
-                                    c.n_heads, s, true, nullptr, 0, rows == batch);
-        else
-            attention_paged<__nv_bfloat16>((__nv_bfloat16 *)m->att, col, (const __nv_bfloat16 *)m->q, col, seq, pos,
-                                           rows, max_len, kv, c.n_heads, s, true, nullptr, 0, rows == batch);
-        ++launches;
+        {
+            // decode rows may split the context over several CTAs (split-K attention)
+            const AttnSplitWs *ws = rows == batch ? &m->attn_ws : nullptr;
+            if (m->act == kF16)
+                launches += attention_paged<__half>((__half *)m->att, col, (const __half *)m->q, col, seq, pos, rows,
+                                                    max_len, kv, c.n_heads, s, true, nullptr, 0, rows == batch, ws);
+            else
+                launches += attention_paged<__nv_bfloat16>((__nv_bfloat16 *)m->att, col, (const __nv_bfloat16 *)m->q,
+                                                           col, seq, pos, rows, max_len, kv, c.n_heads, s, true,
+                                                           nullptr, 0, rows == batch, ws);
+        }
         {
             GemvArgs a;
             a.w = L.o;
@@ -563,7 +568,8 @@ void wk_model_destroy(wk_model *m) {
     free(m->vpool);
     void *bufs[] = {m->block_table, m->d_pos, m->d_seq, m->d_ids, m->d_tokens, m->d_row_seq, m->d_row_pos,
                     m->x, m->q, m->att, m->h, m->xn, m->part_val, m->part_key, m->counter,
-                    m->p32, m->win_send, m->win_recv, m->d_mk_layers, m->d_mk_maps, m->d_mk_bar};
+                    m->p32, m->win_send, m->win_recv, m->d_mk_layers, m->d_mk_maps, m->d_mk_bar,
+                    m->attn_ws.scores, m->attn_ws.mpart, m->attn_ws.opart, m->attn_ws.counter};
     for (void *p : bufs)
         if (p) cudaFree(p);
     free(m->layers);
@@ -614,6 +620,20 @@ int wk_model_alloc_cache(wk_model *m, int max_batch, int max_ctx) {
     for (int **p : {&m->d_pos, &m->d_seq, &m->d_ids, &m->d_tokens}) WK_TRY(cudaMallocAsync(p, sizeof(int) * max_batch, s));
     iota_kernel<<<(max_batch + 127) / 128, 128, 0, s>>>(m->d_seq, max_batch, 0, 1);
     WK_TRY(cudaGetLastError());
+    {
+        // split-K decode attention: up to 64 splits of the context per (sequence, kv head)
+        AttnSplitWs &w = m->attn_ws;
+        w.max_rows = max_batch;
+        w.max_kv_heads = c.n_kv_heads;
+        w.max_splits = 64;
+        w.lpad = m->max_pages * kPage;
+        const size_t rh = (size_t)max_batch * c.n_kv_heads;
+        WK_TRY(cudaMallocAsync(&w.scores, rh * 8 * w.lpad * act_size(m->act), s));
+        WK_TRY(cudaMallocAsync((void **)&w.mpart, rh * w.max_splits * 8 * sizeof(float), s));
+        WK_TRY(cudaMallocAsync((void **)&w.opart, rh * w.max_splits * 8 * c.head_dim * sizeof(float), s));
+        WK_TRY(cudaMallocAsync((void **)&w.counter, rh * sizeof(int), s));
+        WK_TRY(cudaMemsetAsync(w.counter, 0, rh * sizeof(int), s));
+    }
     if (m->tp) {
         WK_TRY(cudaMallocAsync(&m->win_send, tp_winner_chunk(max_batch), s));
         WK_TRY(cudaMallocAsync(&m->win_recv, tp_winner_chunk(max_batch) * tp_world(), s));

@@ -129,13 +129,23 @@ struct PagedKV {
     const int *block_table = nullptr;  // [seqs][max_pages]
     int max_pages = 0, page = 0, kv_heads = 0, hd = 0;
 };
+// Scratch of split-K decode attention (sized by its owner; counter zeroed once).
+struct AttnSplitWs {
+    void *scores = nullptr;     // [max_rows][max_kv_heads][8][lpad] (type T)
+    float *mpart = nullptr;     // [max_rows][max_kv_heads][max_splits][8]
+    float *opart = nullptr;     // [max_rows][max_kv_heads][max_splits][8][head_dim]
+    int *counter = nullptr;     // [max_rows][max_kv_heads], zero between launches
+    int max_rows = 0, max_kv_heads = 0, max_splits = 0, lpad = 0;
+};
+// Returns the number of kernel launches.
 // early: every row is the newest token of its sequence and older pages were
 // written by earlier launches (decode), so they may be fetched before the
 // programmatic-dependent-launch wait.
 template <typename T>
-void attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
+int attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
                      int nrows, int max_len, const PagedKV &c, int H, cudaStream_t s, bool pdl,
-                     const void *pf = nullptr, long pf_bytes = 0, bool early = false);
+                     const void *pf = nullptr, long pf_bytes = 0, bool early = false,
+                     const AttnSplitWs *ws = nullptr);
 template <typename T>
 void attention_qkv_rows(T *out, const T *qkv, int B, int Tn, int NH, int kvNH, int HS, cudaStream_t s);
 
