@@ -92,6 +92,10 @@ int wk_tp_init(int rank, int world, const void *id);
 void wk_tp_fini(void);
 int wk_tp_rank(void);
 int wk_tp_world(void);
+/* 1 when the ranks exchange decode-sized partials through each other's memory
+ * (one fused all-reduce + residual launch over NVLink), 0 when they use NCCL
+ * (WUKONG_TP_P2P=0, or a rank could not map the others' buffers) */
+int wk_tp_p2p(void);
 int wk_model_set_tp(wk_model *m, int enable);
 
 /* No counterpart in the reference.  cuda_predict without device allocation,

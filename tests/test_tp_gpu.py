@@ -46,8 +46,9 @@ def _run(engine_cfg, layers, w, tp):
     return toks
 
 
-def _worker(rank, world, uid, q):
+def _worker(rank, world, uid, q, p2p):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["WUKONG_TP_P2P"] = p2p
     try:
         from tests.gpu_util import up
         from wukong_b200 import tp
@@ -61,13 +62,17 @@ def _worker(rank, world, uid, q):
             layers.append({k: up(v) for k, v in s.items()})
         wo = dict(w, output=tp.shard_output(w["output"], CFG, wk.Q8_0, rank, world))
         toks = _run(tp.local_config(CFG, world), layers, wo, tp=True)
+        used = L.wk_tp_p2p()
         L.wk_tp_fini()
-        q.put((rank, toks))
+        q.put((rank, (toks, used)))
     except Exception as e:  # reported to the parent
         q.put((rank, f"{type(e).__name__}: {e}"))
 
 
-def test_tp2_engine_matches_single_gpu(dev):
+@pytest.mark.parametrize("p2p", ["1", "0"])
+def test_tp2_engine_matches_single_gpu(dev, p2p):
+    """p2p=1: partials exchanged through peer memory in one fused launch;
+    p2p=0: NCCL all-reduce and all-gather."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("tensor parallelism needs 2 GPUs")
@@ -77,7 +82,7 @@ def test_tp2_engine_matches_single_gpu(dev):
     wk.check(dev.wk_tp_unique_id(uid))
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, uid.raw, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, uid.raw, q, p2p)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}
@@ -105,7 +110,9 @@ def test_tp2_engine_matches_single_gpu(dev):
     layers = [{k: up(v) for k, v in lw.items()} for lw in fused_for_oracle(w)["layers"]]
     ref = _run(CFG, layers, w, tp=False)
     assert set(got) == {0, 1}, f"ranks reported {sorted(got)}; exit codes {[p.exitcode for p in procs]}"
-    assert isinstance(got[0], list), got[0]
-    assert isinstance(got[1], list), got[1]
-    assert got[0] == got[1]
-    assert got[0] == ref
+    assert isinstance(got[0], tuple), got[0]
+    assert isinstance(got[1], tuple), got[1]
+    (t0, used0), (t1, used1) = got[0], got[1]
+    assert used0 == used1 == int(p2p)
+    assert t0 == t1
+    assert t0 == ref

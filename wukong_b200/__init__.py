@@ -75,6 +75,7 @@ EXT = {
     "wk_tp_fini": (None, []),
     "wk_tp_rank": (_I, []),
     "wk_tp_world": (_I, []),
+    "wk_tp_p2p": (_I, []),
     "wk_model_set_tp": (_I, [_P, _I]),
 }
 

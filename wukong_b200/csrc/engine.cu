@@ -229,12 +229,8 @@ int ensure_rows(wk_model *m, int rows) {
 // the residual stream.  Returns the number of this library's kernel launches.
 int reduce_partials(wk_model *m, int rows, cudaStream_t s) {
     const long n = (long)rows * m->cfg.d_model;
-    tp_allreduce_f32(m->p32, (size_t)n, s);
-    if (m->act == kF16)
-        resid_from_partial<__half>((__half *)m->x, m->p32, n, s);
-    else
-        resid_from_partial<__nv_bfloat16>((__nv_bfloat16 *)m->x, m->p32, n, s);
-    return 1;
+    if (m->act == kF16) return allreduce_resid<__half>((__half *)m->x, m->p32, n, s);
+    return allreduce_resid<__nv_bfloat16>((__nv_bfloat16 *)m->x, m->p32, n, s);
 }
 
 // Run the layers and the logits head on `rows` activation rows in m->x.

@@ -88,6 +88,204 @@ __global__ void argmax_combine_kernel(int *__restrict__ tokens, const uint8_t *_
     tokens[b] = logits_index(bk, pack);
 }
 
+// ---------------------------------------------------------------- one-shot exchange over peer memory
+// Each rank exports one buffer (CUDA IPC) that all ranks map:
+//   [0, 256)                 all-reduce flags [2 parities][16 CTAs] (u64 epochs)
+//   [256, 512)               winner flags [2 parities] (u64 epochs)
+//   [512, +2 kArSlot)        all-reduce payload, one slot per parity (fp32)
+//   [.., +2 kWinSlot)        logits winners, one slot per parity
+// A rank writes its payload into its own slot, publishes the epoch in its own
+// flag (release, system scope), waits (bounded) for every peer's flag of the
+// same CTA and parity, and reads the peers' slots directly over NVLink.  The
+// parity alternates per call: a rank reuses a slot two calls later, when every
+// peer has already waited for its next call's flags, so no reader is left.
+constexpr int kArCtas = 16;
+constexpr size_t kArSlot = 256 * 1024;
+constexpr size_t kWinSlot = 4096;
+constexpr size_t kP2POff = 512;
+constexpr size_t kP2PBytes = kP2POff + 2 * kArSlot + 2 * kWinSlot;
+constexpr int kMaxWorld = 8;
+
+struct P2P {
+    bool ok = false;
+    uint8_t *mine = nullptr;              // this rank's exported buffer
+    uint8_t *peers_h[kMaxWorld] = {};     // mapped buffers of all ranks (own included)
+    uint8_t **peers_d = nullptr;          // the same, on the device
+    unsigned long long *epochs = nullptr; // per-CTA call counters [kArCtas + 1], device
+};
+P2P g_p2p;
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Wait until *flag == e; false (error recorded) after one second.
+__device__ bool wait_flag(const unsigned long long *flag, unsigned long long e, int *err, int code) {
+    if (ld_acquire_sys(flag) >= e) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(flag) < e) {
+        if (globaltimer_ns() - t0 > 1000000000ull) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+        __nanosleep(32);
+    }
+    return true;
+}
+
+// x = T(x + T(sum over ranks of partial)) for n values; CTA c owns values [c n/k, (c+1) n/k).
+template <typename T>
+__global__ void __launch_bounds__(512) p2p_allreduce_resid_kernel(T *__restrict__ x, const float *__restrict__ partial,
+                                                                  long n, uint8_t *const *peers, int rank, int world,
+                                                                  unsigned long long *epochs, int *err) {
+    __shared__ unsigned long long e_s;
+    __shared__ int ok_s;
+    const int c = blockIdx.x, tid = threadIdx.x;
+    const long per = (n + gridDim.x - 1) / gridDim.x;
+    const long lo = c * per, hi = min(n, lo + per);
+    if (tid == 0) {
+        e_s = ++epochs[c];
+        ok_s = 1;
+    }
+    __syncthreads();
+    const unsigned long long e = e_s;
+    const int par = (int)(e & 1);
+    float *mine = reinterpret_cast<float *>(peers[rank] + kP2POff + par * kArSlot);
+    for (long i = lo + tid; i < hi; i += blockDim.x) mine[i] = partial[i];
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<unsigned long long *>(peers[rank]) + par * kArCtas + c, e);
+    }
+    if (tid < world && !wait_flag(reinterpret_cast<const unsigned long long *>(peers[tid]) + par * kArCtas + c, e,
+                                  err, 40))
+        ok_s = 0;
+    __syncthreads();
+    if (!ok_s) return;
+    for (long i = lo + tid; i < hi; i += blockDim.x) {
+        float acc = 0.f;
+        for (int r = 0; r < world; ++r)
+            acc += __ldcv(reinterpret_cast<const float *>(peers[r] + kP2POff + par * kArSlot) + i);
+        x[i] = from_float<T>(to_float(x[i]) + round_to<T>(acc));
+    }
+}
+
+// Logits winners: keys [B] u64 and values [B] f32 of every rank -> token ids.
+__global__ void __launch_bounds__(32) p2p_argmax_kernel(int *__restrict__ tokens, const uint8_t *__restrict__ send, int B,
+                                                        int pack, uint8_t *const *peers, int rank, int world,
+                                                        unsigned long long *epochs, int *err) {
+    __shared__ unsigned long long e_s;
+    __shared__ int ok_s;
+    const int tid = threadIdx.x;
+    const size_t bytes = ((size_t)B * 12 + 15) / 16 * 16;  // keys [B] u64, then values [B] f32
+    if (tid == 0) {
+        e_s = ++epochs[kArCtas];
+        ok_s = 1;
+    }
+    __syncthreads();
+    const unsigned long long e = e_s;
+    const int par = (int)(e & 1);
+    uint8_t *mine = peers[rank] + kP2POff + 2 * kArSlot + par * kWinSlot;
+    for (size_t i = tid * 4; i < bytes; i += 32 * 4)
+        *reinterpret_cast<uint32_t *>(mine + i) = *reinterpret_cast<const uint32_t *>(send + i);
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<unsigned long long *>(peers[rank] + 256) + par, e);
+    }
+    if (tid < world && !wait_flag(reinterpret_cast<const unsigned long long *>(peers[tid] + 256) + par, e, err, 41))
+        ok_s = 0;
+    __syncthreads();
+    if (!ok_s) return;
+    for (int b = tid; b < B; b += 32) {
+        float bv = -INFINITY;
+        uint64_t bk = ~0ull;
+        for (int r = 0; r < world; ++r) {
+            const uint8_t *rec = peers[r] + kP2POff + 2 * kArSlot + par * kWinSlot;
+            const uint64_t k = __ldcv(reinterpret_cast<const unsigned long long *>(rec) + b);
+            const float v = __ldcv(reinterpret_cast<const float *>(rec + 8L * B) + b);
+            if (k == ~0ull) continue;
+            if (v > bv || (v == bv && k < bk)) {
+                bv = v;
+                bk = k;
+            }
+        }
+        tokens[b] = logits_index(bk, pack);
+    }
+}
+
+// Map every rank's exchange buffer (collective: all ranks call it after the
+// communicator exists).  Returns false on every rank if any rank failed.
+bool p2p_setup() {
+    bool ok = g_world <= kMaxWorld;
+    const char *env = getenv("WUKONG_TP_P2P");
+    if (env && env[0] == '0') ok = false;
+    cudaIpcMemHandle_t mine_h = {};
+    if (ok) ok = cudaMalloc(&g_p2p.mine, kP2PBytes) == cudaSuccess &&
+                 cudaMemset(g_p2p.mine, 0, kP2PBytes) == cudaSuccess &&
+                 cudaIpcGetMemHandle(&mine_h, g_p2p.mine) == cudaSuccess;
+    // exchange handles (and the local verdict) through the communicator
+    struct Rec {
+        cudaIpcMemHandle_t h;
+        int ok;
+        int pad[15];
+    };
+    Rec rec = {};
+    rec.h = mine_h;
+    rec.ok = ok ? 1 : 0;
+    Rec *d = nullptr;
+    Rec *all = (Rec *)calloc(g_world, sizeof(Rec));
+    cudaStream_t s = stream();
+    WK_CHECK(cudaMalloc(&d, sizeof(Rec) * (g_world + 1)));
+    WK_CHECK(cudaMemcpy(d + g_world, &rec, sizeof(Rec), cudaMemcpyHostToDevice));
+    nccl_check(g_nccl.all_gather(d + g_world, d, sizeof(Rec), ncclUint8, g_comm, s), "ncclAllGather");
+    WK_CHECK(cudaStreamSynchronize(s));
+    WK_CHECK(cudaMemcpy(all, d, sizeof(Rec) * g_world, cudaMemcpyDeviceToHost));
+    cudaFree(d);
+    for (int r = 0; r < g_world; ++r) ok = ok && all[r].ok;
+    for (int r = 0; ok && r < g_world; ++r) {
+        if (r == g_rank) {
+            g_p2p.peers_h[r] = g_p2p.mine;
+            continue;
+        }
+        void *pp = nullptr;
+        ok = cudaIpcOpenMemHandle(&pp, all[r].h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        g_p2p.peers_h[r] = (uint8_t *)pp;
+    }
+    free(all);
+    // every rank must agree before any kernel relies on the mappings
+    int *flag = nullptr;
+    int v = ok ? 1 : 0;
+    WK_CHECK(cudaMalloc(&flag, sizeof(int)));
+    WK_CHECK(cudaMemcpy(flag, &v, sizeof(int), cudaMemcpyHostToDevice));
+    nccl_check(g_nccl.all_reduce(flag, flag, 1, ncclInt32, ncclMin, g_comm, s), "ncclAllReduce");
+    WK_CHECK(cudaStreamSynchronize(s));
+    WK_CHECK(cudaMemcpy(&v, flag, sizeof(int), cudaMemcpyDeviceToHost));
+    cudaFree(flag);
+    ok = v == 1;
+    if (ok) ok = cudaMalloc(&g_p2p.peers_d, sizeof(uint8_t *) * kMaxWorld) == cudaSuccess &&
+                 cudaMemcpy(g_p2p.peers_d, g_p2p.peers_h, sizeof(uint8_t *) * kMaxWorld, cudaMemcpyHostToDevice) ==
+                     cudaSuccess &&
+                 cudaMalloc(&g_p2p.epochs, sizeof(unsigned long long) * (kArCtas + 1)) == cudaSuccess &&
+                 cudaMemset(g_p2p.epochs, 0, sizeof(unsigned long long) * (kArCtas + 1)) == cudaSuccess;
+    cudaGetLastError();
+    g_p2p.ok = ok;
+    return ok;
+}
+
+void p2p_teardown() {
+    for (int r = 0; r < kMaxWorld; ++r)
+        if (g_p2p.peers_h[r] && g_p2p.peers_h[r] != g_p2p.mine) cudaIpcCloseMemHandle(g_p2p.peers_h[r]);
+    if (g_p2p.mine) cudaFree(g_p2p.mine);
+    if (g_p2p.peers_d) cudaFree(g_p2p.peers_d);
+    if (g_p2p.epochs) cudaFree(g_p2p.epochs);
+    g_p2p = P2P();
+}
+
 }  // namespace
 
 bool tp_active() { return g_comm != nullptr && g_world > 1; }
@@ -102,11 +300,34 @@ size_t tp_winner_chunk(int B) { return ((size_t)B * 12 + 15) / 16 * 16; }
 
 void tp_argmax_combine(int *tokens, const void *send, void *recv, int B, int pack, cudaStream_t s) {
     const size_t chunk = tp_winner_chunk(B);
+    if (g_p2p.ok && chunk <= kWinSlot) {
+        p2p_argmax_kernel<<<1, 32, 0, s>>>(tokens, (const uint8_t *)send, B, pack, g_p2p.peers_d, g_rank, g_world,
+                                           g_p2p.epochs, g_rt.d_error);
+        WK_CHECK_LAUNCH();
+        return;
+    }
     nccl_check(g_nccl.all_gather(send, recv, chunk, ncclUint8, g_comm, s), "ncclAllGather");
     argmax_combine_kernel<<<(B + 127) / 128, 128, 0, s>>>(tokens, (const uint8_t *)recv, (long)chunk, B, g_world,
                                                          pack);
     WK_CHECK_LAUNCH();
 }
+
+template <typename T> int allreduce_resid(T *x, float *p, long n, cudaStream_t s) {
+    if (n <= 0) return 0;
+    if (g_p2p.ok && (size_t)n * sizeof(float) <= kArSlot) {
+        // always kArCtas CTAs: every CTA index takes part in every call, so all
+        // CTAs of a call use the same slot parity (see the layout comment)
+        p2p_allreduce_resid_kernel<T><<<kArCtas, 512, 0, s>>>(x, p, n, g_p2p.peers_d, g_rank, g_world, g_p2p.epochs,
+                                                           g_rt.d_error);
+        WK_CHECK_LAUNCH();
+        return 1;
+    }
+    tp_allreduce_f32(p, (size_t)n, s);
+    resid_from_partial<T>(x, p, n, s);
+    return 1;
+}
+template int allreduce_resid<__half>(__half *, float *, long, cudaStream_t);
+template int allreduce_resid<__nv_bfloat16>(__nv_bfloat16 *, float *, long, cudaStream_t);
 
 template <typename T> void resid_from_partial(T *x, const float *p, long n, cudaStream_t s) {
     if (n <= 0) return;
@@ -147,12 +368,14 @@ int wk_tp_init(int rank, int world, const void *id) {
     }
     g_rank = rank;
     g_world = world;
+    p2p_setup();  // the one-shot exchange over peer memory, or NCCL if any rank cannot map the others
     return 0;
 }
 
 void wk_tp_fini(void) {
     if (g_comm) {
         cudaStreamSynchronize(stream());
+        p2p_teardown();
         g_nccl.comm_destroy(g_comm);
     }
     g_comm = nullptr;
@@ -162,5 +385,6 @@ void wk_tp_fini(void) {
 
 int wk_tp_rank(void) { return g_rank; }
 int wk_tp_world(void) { return g_world; }
+int wk_tp_p2p(void) { return g_p2p.ok ? 1 : 0; }
 
 }  // extern "C"

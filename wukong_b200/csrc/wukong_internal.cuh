@@ -212,6 +212,11 @@ size_t tp_winner_chunk(int B);
 void tp_argmax_combine(int *tokens, const void *send, void *recv, int B, int pack, cudaStream_t s);
 // x = T(x + T(p)) over n elements
 template <typename T> void resid_from_partial(T *x, const float *p, long n, cudaStream_t s);
+// Sum the fp32 partials p of all ranks and add them to the residual stream:
+// x = T(x + T(sum)).  One fused launch over peer memory when the exchange is
+// mapped (decode sizes), else NCCL all-reduce + residual kernel.  Returns this
+// library's kernel launches.
+template <typename T> int allreduce_resid(T *x, float *p, long n, cudaStream_t s);
 
 // ---------------------------------------------------------------- engine.cu
 // Records the message returned by wk_last_error() and returns -1.
