@@ -39,10 +39,10 @@ def _decode(monkeypatch, mk, dm, w, cfg, B, ctx, ids, steps):
 
 
 @pytest.mark.parametrize("D,B,F,V", [(64, 1, 1024, 2000), (64, 3, 1024, 2000), (64, 8, 1024, 2000),
-                                     (128, 2, 1024, 3000), (64, 2, 8192, 16400)])
+                                     (128, 2, 1024, 3000), (64, 2, 8192, 65600)])
 def test_persistent_decode_equals_graph_path(dev, monkeypatch, D, B, F, V):
-    """F = 8192 / V = 16400 reach the warp-tile mode (>= 1024 tiles) of the
-    SwiGLU and logits layers; the smaller shapes split tiles over a CTA."""
+    """V = 65600 (4100 tiles) reaches the warp-tile mode of the logits layer
+    (>= 4096 tiles by default); the other layers split tiles over a CTA."""
     H, Hk = 8, 2
     cfg = dict(L=2, d=H * D, H=H, Hk=Hk, D=D, F=F, V=V, eps=1e-5, theta=500000.0)
     ctx, n, steps = 96, 40, 30  # positions 40..70 cross the 64-token page

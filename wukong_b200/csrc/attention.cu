@@ -516,6 +516,7 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
     uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnSlots * kPageBytes);
     float *Ms = reinterpret_cast<float *>(bars + kAttnSlots);  // [8]
     T *pl = reinterpret_cast<T *>(Ms + 8);                     // [8][pps * 64] this split's P
+    T *ss = pl + 8 * pps * kAttnPage;                          // [8][Lpad] the row's scores (staged)
     __shared__ int last;
     const int kvh = blockIdx.x, row = blockIdx.y, z = blockIdx.z, nz = gridDim.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -555,10 +556,20 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
         Ms[tid] = m;
     }
     __syncthreads();
+    // the row's scores into shared memory with 16-byte loads (one round trip)
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(S + rh * 8 * lpad);
+        const int per_head = Lpad * (int)sizeof(T) / 16, stride = lpad * (int)sizeof(T) / 16;
+        for (int i = tid; i < 8 * per_head; i += 128) {
+            const int h = i / per_head, c = i - h * per_head;
+            reinterpret_cast<uint4 *>(ss)[h * per_head + c] = src[h * stride + c];
+        }
+    }
+    __syncthreads();
     // softmax over the whole row, in the single-CTA kernel's order
     {
         const int h = tid >> 4, i0 = tid & 15;
-        const T *sr = S + (rh * 8 + h) * lpad;
+        const T *sr = ss + h * Lpad;
         const float M = Ms[h];
         float lsum = 0.f;
         for (int j = i0; j < Lpad; j += 16)
@@ -662,7 +673,8 @@ bool launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_
     if (nz < 2) return false;
     const float scale = 1.0f / sqrtf((float)D);
     const size_t smem_a = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 32 * 4 + 8 * D * 2;
-    const size_t smem_b = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 8 * 4 + (size_t)8 * pps * kAttnPage * 2;
+    const size_t smem_b = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 8 * 4 +
+                          (size_t)8 * pps * kAttnPage * 2 + (size_t)8 * pages * kAttnPage * 2;
     if ((int)smem_b > g_rt.max_smem_optin) return false;
     auto ka = attn_split_scores_kernel<T, D>;
     auto kb = attn_split_pv_kernel<T, D>;

@@ -69,6 +69,7 @@ struct Runtime {
     size_t ws_size = 0;
     bool pdl = true;      // programmatic dependent launch on the hot kernels
     bool tc_gemm = true;  // tcgen05 GEMM for activation blocks of >= 16 rows
+    int warp_tile_min = 4096;  // SwiGLU / logits layers with this many 16-row tiles run one tile per warp
 };
 extern Runtime g_rt;
 

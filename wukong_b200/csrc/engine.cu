@@ -486,6 +486,7 @@ void mk_setup(wk_model *m) {
     a.part_key = m->part_key;
     a.bar = m->d_mk_bar;
     a.err = g_rt.d_error;
+    a.warp_tile_min = g_rt.warp_tile_min;
     m->mk = a;
     m->mk_stages = S;
     m->mk_smem = smem;
@@ -556,6 +557,7 @@ void wk_model_destroy(wk_model *m) {
     cudaStream_t s = stream();
     cudaStreamSynchronize(s);
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->d_mk_maps) mk_forget_maps(m->d_mk_maps);
     for (int l = 0; m->kpool && l < m->cfg.n_layers; ++l) {
         cudaFree(m->kpool[l]);
         cudaFree(m->vpool[l]);

@@ -240,20 +240,23 @@ __device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad) {
     }
 }
 
-// Threads 0..127 own one (row r, column m) output of the 16 x 8 tile.
+// Threads 0..127 own one (row r, column m) output of the 16 x 8 tile; `red`
+// holds the 8 warps' partial tiles.  Partner rows (RoPE pairs, up / gate) are
+// summed by the thread itself in the same warp order, so no second reduction
+// pass (and no extra barrier) is needed.
+__device__ __forceinline__ float tile_sum(const float *red, int r, int m) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) acc += red[(w * 16 + r) * 8 + m];
+    return acc;
+}
+
 template <typename T>
-__device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float &best_v, uint64_t &best_k) {
+__device__ void epilogue(const GemvArgs &a, const float *red, int tile, float &best_v, uint64_t &best_k) {
     const int tid = threadIdx.x;
     const int r = (tid >> 3) & 15, m = tid & 7;
-    float acc = 0.f;
-    if (tid < 128) {
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) acc += sm.red[(w * 16 + r) * 8 + m];
-    }
-    __syncthreads();
-    if (tid < 128) sm.red[r * 8 + m] = acc;  // reduced tile in the slot of warp 0
-    __syncthreads();
     if (tid >= 128 || m >= a.M || !row_valid(a, tile, r)) return;
+    float acc = tile_sum(red, r, m);
     const int n = tile_row(a, tile, r);
     switch (a.epi) {
     case EPI_STORE: {
@@ -271,7 +274,7 @@ __device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float &bes
         const float y = round_to<T>(acc);
         const int pos = a.pos[m];
         if (n < a.nq + a.nk) {
-            const float yp = round_to<T>(sm.red[(r ^ 1) * 8 + m]);
+            const float yp = round_to<T>(tile_sum(red, r ^ 1, m));
             const int dd = (n - (n < a.nq ? 0 : a.nq)) % a.hd;
             const float *f = a.freqs + (long)pos * a.hd + (dd & ~1);
             const float cs = f[0], sn = f[1];
@@ -295,7 +298,7 @@ __device__ void epilogue(const GemvArgs &a, const Smem &sm, int tile, float &bes
     case EPI_SWIGLU: {
         if (r < 8) {
             const float u = round_to<T>(acc);
-            const float gt = round_to<T>(sm.red[(r + 8) * 8 + m]);
+            const float gt = round_to<T>(tile_sum(red, r + 8, m));
             const float sig = 1.0f / (1.0f + expf(-gt));
             reinterpret_cast<T *>(a.out)[(long)m * a.ldo + tile * 8 + r] = from_float<T>((gt * sig) * u);
         }
@@ -393,7 +396,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
 
     // this warp's unit sequence.  CTA tiles: tiles blockIdx.x, +gridDim.x, ...,
     // chunks w, w + 8, ...; warp tiles: tiles gw, gw + 8 gridDim.x, ..., all chunks
-    const bool wmode = warp_tiles(a.epi, ntiles);
+    const bool wmode = warp_tiles(a.epi, ntiles, a.warp_tile_min);
     const int gw = blockIdx.x * kWarps + w, nw = gridDim.x * kWarps;
     const int cstart = wmode ? 0 : w, cstep = wmode ? 1 : kWarps, tstep = wmode ? nw : (int)gridDim.x;
     int p_tile = wmode ? gw : (int)blockIdx.x, p_chunk = cstart;  // producer cursor
@@ -490,8 +493,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         red[(g + 8) * 8 + 2 * t] = c[0][2] + c[1][2];
         red[(g + 8) * 8 + 2 * t + 1] = c[0][3] + c[1][3];
         __syncthreads();
-        epilogue<T>(a, sm, tile, best_v, best_k);
-        __syncthreads();
+        epilogue<T>(a, sm.red, tile, best_v, best_k);
+        __syncthreads();  // red is rewritten by the next tile
     }
 
     if (a.epi == EPI_LOGITS) {
@@ -600,6 +603,7 @@ void gemv(GemvArgs a, int act, cudaStream_t s) {
         map = weight_map(a.w, rows, rb, box_inner, a.epi == EPI_SWIGLU ? 8 : kTileRows);
     }
     a.bulk = map ? 1 : 0;
+    a.warp_tile_min = g_rt.warp_tile_min;
     if (map) a.wmap = *map;
     if (!a.err) a.err = g_rt.d_error;
     if (((uintptr_t)a.x % 8) || (a.ldx % 4)) WK_PANIC("gemv: activations must be 8-byte aligned rows");

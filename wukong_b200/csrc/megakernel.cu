@@ -74,7 +74,8 @@ __device__ __forceinline__ Gp gp_of(const MkArgs &a, int gi) {
         }
     }
     p.nchunks = K / 256;
-    p.wm = warp_tiles(p.kind == MK_FC ? EPI_SWIGLU : (p.kind == MK_LOGITS ? EPI_LOGITS : EPI_STORE), p.ntiles);
+    p.wm = warp_tiles(p.kind == MK_FC ? EPI_SWIGLU : (p.kind == MK_LOGITS ? EPI_LOGITS : EPI_STORE), p.ntiles,
+                      a.warp_tile_min);
     return p;
 }
 
@@ -143,10 +144,16 @@ __device__ __forceinline__ void tma_box(void *dst, const CUtensorMap *map, int x
         : "memory");
 }
 
+// Weight tensor maps of the model being decoded, in the constant bank (the TMA
+// unit reads a descriptor per copy; constant memory serves it from the
+// constant cache).  Filled by mk_launch when the model changes.
+constexpr int kMaxMaps = 4 * 112 + 1;  // 112 layers
+__constant__ CUtensorMap c_maps[kMaxMaps];
+
 struct Sm {
     uint8_t *ring;   // [kW][S][kUnit]
     uint64_t *bars;  // [kW][S]
-    float *red;      // [kW][16][8]
+    float *red;      // [2][kW][16][8] partial tiles, alternating per tile
     float *misc;     // [8] norm scales, [128] logits values, then [128] u64 keys
     uint8_t *work;   // normalised X [B][d] half, or the attention buffers
 };
@@ -154,7 +161,7 @@ struct Sm {
 __device__ __forceinline__ void issue_unit(const MkArgs &a, const Sm &sm, const Cursor &c, int w, int S, int slot) {
     uint8_t *dst = sm.ring + (size_t)(w * S + slot) * kUnit;
     uint64_t *bar = sm.bars + w * S + slot;
-    const CUtensorMap *map = a.maps + c.gi;
+    const CUtensorMap *map = c_maps + c.gi;
     mbar_expect_tx(bar, kUnit);
     const int x = c.chunk * (kRowB / 2);  // uint16 column of the box
     if (c.kind == MK_FC) {
@@ -325,20 +332,22 @@ __device__ __forceinline__ void mk_warp_epilogue(const MkArgs &a, int kind, int 
     }
 }
 
-// Fused epilogue of one tile; threads 0..127 own (row r, column m).
-__device__ void mk_epilogue(const MkArgs &a, const Sm &sm, int kind, int l, int tile, float &best_v,
+// Fused epilogue of one tile; threads 0..127 own (row r, column m).  `red`
+// holds the 8 warps' partial tiles; partner rows are summed by the thread in
+// the same warp order (bit-identical to the per-op GEMV).
+__device__ __forceinline__ float mk_tile_sum(const float *red, int r, int m) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kW; ++w) acc += red[(w * 16 + r) * 8 + m];
+    return acc;
+}
+
+__device__ void mk_epilogue(const MkArgs &a, const float *red, int kind, int l, int tile, float &best_v,
                             uint64_t &best_k) {
     const int tid = threadIdx.x;
     const int r = (tid >> 3) & 15, m = tid & 7;
-    float acc = 0.f;
-    if (tid < 128) {
-#pragma unroll
-        for (int w = 0; w < kW; ++w) acc += sm.red[(w * 16 + r) * 8 + m];
-    }
-    __syncthreads();
-    if (tid < 128) sm.red[r * 8 + m] = acc;
-    __syncthreads();
     if (tid >= 128 || m >= a.B) return;
+    const float acc = mk_tile_sum(red, r, m);
     switch (kind) {
     case MK_QKV: {
         const int nq = a.H * a.D, nk = a.Hk * a.D;
@@ -349,7 +358,7 @@ __device__ void mk_epilogue(const MkArgs &a, const Sm &sm, int kind, int l, int 
         const int pos = a.pos[m];
         const long page = a.block_table[(long)a.seq[m] * a.max_pages + pos / kPg];
         if (n < nq + nk) {
-            const float yp = round_to<__half>(sm.red[(r ^ 1) * 8 + m]);
+            const float yp = round_to<__half>(mk_tile_sum(red, r ^ 1, m));
             const int dd = (n - (n < nq ? 0 : nq)) % a.D;
             const float *f = a.freqs + (long)pos * a.D + (dd & ~1);
             const float cs = f[0], sn = f[1];
@@ -380,7 +389,7 @@ __device__ void mk_epilogue(const MkArgs &a, const Sm &sm, int kind, int l, int 
     case MK_FC: {
         if (r < 8 && tile * 8 + r < a.F) {
             const float u = round_to<__half>(acc);
-            const float gt = round_to<__half>(sm.red[(r + 8) * 8 + m]);
+            const float gt = round_to<__half>(mk_tile_sum(red, r + 8, m));
             const float sig = 1.0f / (1.0f + expf(-gt));
             a.h[(long)m * a.F + tile * 8 + r] = __float2half_rn((gt * sig) * u);
         }
@@ -573,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
     sm.ring = smem_raw;
     sm.bars = reinterpret_cast<uint64_t *>(sm.ring + (size_t)kW * S * kUnit);
     sm.red = reinterpret_cast<float *>(sm.bars + kW * S);
-    sm.misc = sm.red + kW * 16 * 8;
+    sm.misc = sm.red + 2 * kW * 16 * 8;
     sm.work = reinterpret_cast<uint8_t *>(sm.misc + 8 + 128 + 2 * 128);
     const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     const unsigned G = gridDim.x;
@@ -598,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
     mk_embed(a);
     grid_sync(a, target += G, sync_code++);
 
-    int consumed = 0, off = 0, offw = 0;
+    int consumed = 0, off = 0, offw = 0, ntile_done = 0;
     bool ok = true;
     float best_v = -INFINITY;  // logits winner of this thread (CTA-split logits)
     uint64_t best_k = ~0ull;
@@ -663,15 +672,18 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
                     cur_next(a, pc, w);
                 }
             }
+            // two partial-tile buffers: tile i + 1 writes the other one, and the
+            // barrier of tile i + 1 orders tile i's epilogue reads before tile i + 2's writes
             const int g = lane >> 2, t = lane & 3;
-            float *red = sm.red + w * 16 * 8;
+            float *rbuf = sm.red + (ntile_done & 1) * kW * 16 * 8;
+            float *red = rbuf + w * 16 * 8;
             red[g * 8 + 2 * t] = c[0][0] + c[1][0];
             red[g * 8 + 2 * t + 1] = c[0][1] + c[1][1];
             red[(g + 8) * 8 + 2 * t] = c[0][2] + c[1][2];
             red[(g + 8) * 8 + 2 * t + 1] = c[0][3] + c[1][3];
             __syncthreads();
-            mk_epilogue(a, sm, p.kind, l, tile, best_v, best_k);
-            __syncthreads();
+            mk_epilogue(a, rbuf, p.kind, l, tile, best_v, best_k);
+            ++ntile_done;
         }
         off = (off + p.ntiles) % (int)G;
     };
@@ -754,7 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1) mk_decode_kernel(const __grid_con
 }
 
 template <int D> size_t smem_for(const MkArgs &a, int S) {
-    const size_t fixed = (size_t)kW * S * kUnit + (size_t)kW * S * 8 + kW * 16 * 8 * 4 + (8 + 128 + 256) * 4;
+    const size_t fixed = (size_t)kW * S * kUnit + (size_t)kW * S * 8 + 2 * kW * 16 * 8 * 4 + (8 + 128 + 256) * 4;
     const size_t xs = (size_t)a.B * a.d * 2;
     const size_t attn = (size_t)kPgSlots * kPg * D * 2 + 8 * D * 2 + (size_t)8 * a.lpad * 2 + 8 * 4 * 4;
     return fixed + (xs > attn ? xs : attn);
@@ -767,7 +779,23 @@ size_t mk_smem_bytes(const MkArgs &a, int stages) {
     return s <= (size_t)g_rt.max_smem_optin ? s : 0;
 }
 
+namespace {
+const CUtensorMap *g_loaded_maps = nullptr;  // the maps now in c_maps
+}  // namespace
+
+void mk_forget_maps(const CUtensorMap *maps) {
+    if (g_loaded_maps == maps) g_loaded_maps = nullptr;
+}
+
 cudaError_t mk_launch(const MkArgs &a, int stages, size_t smem, cudaStream_t s) {
+    if (4 * a.L + 1 > kMaxMaps) return cudaErrorInvalidValue;
+    // the constant bank holds one model's maps: reload when another model launches
+    if (g_loaded_maps != a.maps) {
+        const cudaError_t e = cudaMemcpyToSymbolAsync(c_maps, a.maps, sizeof(CUtensorMap) * (4 * a.L + 1), 0,
+                                                      cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return e;
+        g_loaded_maps = a.maps;
+    }
     auto kern = a.D == 64 ? mk_decode_kernel<64> : mk_decode_kernel<128>;
     static size_t configured[2] = {0, 0};
     size_t &cf = configured[a.D == 64 ? 0 : 1];

@@ -5,6 +5,7 @@
 // copies synchronous.  Errors abort the process with a message, as the
 // reference's panic macro does (wukong.h:173-188).
 #include <stdarg.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "wukong_internal.cuh"
@@ -90,6 +91,8 @@ void cuda_init(int idx) {
     g_rt.pdl = !(pdl && pdl[0] == '0');
     const char *tc = getenv("WUKONG_TC_GEMM");
     g_rt.tc_gemm = !(tc && tc[0] == '0');
+    const char *wt = getenv("WUKONG_WARP_TILE_MIN");
+    if (wt && atoi(wt) > 0) g_rt.warp_tile_min = atoi(wt);
     printf("Running on GPU %d: %s, Compute Capability %d.%d\n", idx, prop.name, prop.major, prop.minor);
     fflush(stdout);
     layers_init();

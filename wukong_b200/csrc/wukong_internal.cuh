@@ -62,19 +62,19 @@ struct GemvArgs {
     int *err = nullptr;
     int bulk = 1;  // set by gemv(): 1 when the weight tiles stream by TMA
     int pdl = 1;   // launch with programmatic dependent launch
+    int warp_tile_min = 1 << 30;  // set by gemv() from g_rt.warp_tile_min
 };
 static_assert(alignof(GemvArgs) >= 64, "the tensor map must stay 64-byte aligned");
 
 bool gemv_supported(int wtype, int act, int K);
-// Linear layers with many 16-row tiles (the SwiGLU up|gate layer and the logits
-// of Llama-sized models) give each warp whole tiles: all K-chunks accumulate in
-// one warp, in K order, and the warp applies the epilogue itself.  Fewer tiles
-// are split over the 8 warps of a CTA by K-chunk and reduced in shared memory.
-// The rule depends only on the layer shape, so the per-op GEMV and the
-// persistent decode kernel round identically.
-constexpr int kWarpTileMin = 1024;
-__host__ __device__ inline bool warp_tiles(int epi, int ntiles) {
-    return (epi == EPI_SWIGLU || epi == EPI_LOGITS) && ntiles >= kWarpTileMin;
+// Linear layers with many 16-row tiles (the logits of Llama-sized models) give
+// each warp whole tiles: all K-chunks accumulate in one warp, in K order, and
+// the warp applies the epilogue itself.  Fewer tiles are split over the 8 warps
+// of a CTA by K-chunk and reduced in shared memory.  The rule depends only on
+// the layer shape and the process-wide threshold (g_rt.warp_tile_min), so the
+// per-op GEMV and the persistent decode kernel round identically.
+__host__ __device__ inline bool warp_tiles(int epi, int ntiles, int min_tiles) {
+    return (epi == EPI_SWIGLU || epi == EPI_LOGITS) && ntiles >= min_tiles;
 }
 void gemv(GemvArgs a, int act, cudaStream_t s);
 
@@ -187,6 +187,7 @@ struct MkArgs {
     __half *x, *q, *att, *h;        // activations [B][d], [B][H D], [B][H D], [B][F]
     float *part_val;                // [grid][8] logits winners per CTA
     unsigned long long *part_key;
+    int warp_tile_min;              // g_rt.warp_tile_min (see warp_tiles)
     unsigned long long *bar;        // grid barrier counter (monotonic across launches)
     unsigned long long bar_base;    // its value when this launch starts
     int *err;
@@ -197,6 +198,8 @@ inline int mk_barriers(int L) { return 5 * L + 2; }
 size_t mk_smem_bytes(const MkArgs &a, int stages);
 // Cooperative launch on every SM; an error (nothing launched) when the device cannot co-schedule it.
 cudaError_t mk_launch(const MkArgs &a, int stages, size_t smem, cudaStream_t s);
+// A model's map table is being freed: the next launch reloads the constant bank.
+void mk_forget_maps(const CUtensorMap *maps);
 
 // ---------------------------------------------------------------- tp.cu
 // Tensor parallelism over NCCL (one process per GPU); inactive until wk_tp_init.
