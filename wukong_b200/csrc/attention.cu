@@ -408,7 +408,8 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
                                                                 const int *__restrict__ seq_of_row,
                                                                 const int *__restrict__ pos_of_row, KVPaged kv, int G,
                                                                 int pps, int lpad, float scale, T *__restrict__ S,
-                                                                float *__restrict__ mpart, int *err, int early) {
+                                                                float *__restrict__ mpart, float *__restrict__ minv,
+                                                                int *__restrict__ counter, int *err, int early) {
     constexpr int kPageBytes = kAttnPage * D * 2;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *ring = smem;
@@ -498,9 +499,48 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
         red[(2 * t + 1) * 4 + warp] = mx1;
     }
     __syncthreads();
+    const long rh = (long)row * kv.kv_heads + kvh;
     if (tid < 8)
-        mpart[(((long)row * kv.kv_heads + kvh) * nz + z) * 8 + tid] =
+        mpart[(rh * nz + z) * 8 + tid] =
             fmaxf(fmaxf(red[tid * 4], red[tid * 4 + 1]), fmaxf(red[tid * 4 + 2], red[tid * 4 + 3]));
+    // the last split of this (row, head) computes the softmax normaliser of the
+    // whole row, in the single-CTA kernel's order, for the P.V launch
+    __shared__ int last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(counter + rh, 1) == nz - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int Lpad = npages * kAttnPage;
+    T *ss = reinterpret_cast<T *>(qs + 8 * D);  // [8][Lpad] staged scores
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(S + rh * 8 * lpad);
+        const int per_head = Lpad * (int)sizeof(T) / 16, stride = lpad * (int)sizeof(T) / 16;
+        for (int i = tid; i < 8 * per_head; i += 128) {
+            const int h = i / per_head, c = i - h * per_head;
+            reinterpret_cast<uint4 *>(ss)[h * per_head + c] = __ldcg(src + h * stride + c);
+        }
+    }
+    float *Ms = red;  // [8]
+    if (tid < 8) {
+        float m = -INFINITY;
+        for (int zz = 0; zz < nz; ++zz) m = fmaxf(m, __ldcg(mpart + (rh * nz + zz) * 8 + tid));
+        Ms[tid] = m;
+    }
+    __syncthreads();
+    const int h = tid >> 4, i0 = tid & 15;
+    const float M = Ms[h];
+    float lsum = 0.f;
+    for (int j = i0; j < Lpad; j += 16)
+        if (j < L && h < G) lsum += expf(to_float(ss[h * Lpad + j]) * scale - M);
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (i0 == 0) {
+        minv[rh * 16 + 2 * h] = M;
+        minv[rh * 16 + 2 * h + 1] = 1.0f / lsum;
+    }
+    if (tid == 0) counter[rh] = 0;
 }
 
 template <typename T, int D>
@@ -508,15 +548,13 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
                                                             const int *__restrict__ seq_of_row,
                                                             const int *__restrict__ pos_of_row, KVPaged kv, int G,
                                                             int pps, int lpad, float scale, const T *__restrict__ S,
-                                                            const float *__restrict__ mpart, float *__restrict__ opart,
+                                                            const float *__restrict__ minv, float *__restrict__ opart,
                                                             int *__restrict__ counter, int *err, int early) {
     constexpr int kPageBytes = kAttnPage * D * 2;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *ring = smem;
     uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnSlots * kPageBytes);
-    float *Ms = reinterpret_cast<float *>(bars + kAttnSlots);  // [8]
-    T *pl = reinterpret_cast<T *>(Ms + 8);                     // [8][pps * 64] this split's P
-    T *ss = pl + 8 * pps * kAttnPage;                          // [8][Lpad] the row's scores (staged)
+    T *pl = reinterpret_cast<T *>(bars + kAttnSlots);  // [8][pps * 64] this split's P
     __shared__ int last;
     const int kvh = blockIdx.x, row = blockIdx.y, z = blockIdx.z, nz = gridDim.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -550,37 +588,16 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
             bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
         }
     const long rh = (long)row * kv.kv_heads + kvh;
-    if (tid < 8) {
-        float m = -INFINITY;
-        for (int zz = 0; zz < nz; ++zz) m = fmaxf(m, mpart[(rh * nz + zz) * 8 + tid]);
-        Ms[tid] = m;
-    }
-    __syncthreads();
-    // the row's scores into shared memory with 16-byte loads (one round trip)
-    {
-        const uint4 *src = reinterpret_cast<const uint4 *>(S + rh * 8 * lpad);
-        const int per_head = Lpad * (int)sizeof(T) / 16, stride = lpad * (int)sizeof(T) / 16;
-        for (int i = tid; i < 8 * per_head; i += 128) {
-            const int h = i / per_head, c = i - h * per_head;
-            reinterpret_cast<uint4 *>(ss)[h * per_head + c] = src[h * stride + c];
-        }
-    }
-    __syncthreads();
-    // softmax over the whole row, in the single-CTA kernel's order
+    // P of this split's keys: T(T(e_j) / sum) with the row's max and sum from the scores launch
     {
         const int h = tid >> 4, i0 = tid & 15;
-        const T *sr = ss + h * Lpad;
-        const float M = Ms[h];
-        float lsum = 0.f;
-        for (int j = i0; j < Lpad; j += 16)
-            if (j < L && h < G) lsum += expf(to_float(sr[j]) * scale - M);
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-        const float inv = 1.0f / lsum;
+        const T *sr = S + (rh * 8 + h) * lpad;
+        const float M = minv[rh * 16 + 2 * h], inv = minv[rh * 16 + 2 * h + 1];
         for (int jj = i0; jj < n * kAttnPage; jj += 16) {
             const int j = p0 * kAttnPage + jj;
             float pv = 0.f;
-            if (j < L && h < G) pv = to_float(from_float<T>(to_float(from_float<T>(expf(to_float(sr[j]) * scale - M))) * inv));
+            if (j < L && h < G)
+                pv = to_float(from_float<T>(to_float(from_float<T>(expf(to_float(sr[j]) * scale - M))) * inv));
             pl[h * wl + jj] = from_float<T>(pv);
         }
     }
@@ -672,10 +689,10 @@ bool launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_
     nz = (pages + pps - 1) / pps;
     if (nz < 2) return false;
     const float scale = 1.0f / sqrtf((float)D);
-    const size_t smem_a = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 32 * 4 + 8 * D * 2;
-    const size_t smem_b = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 8 * 4 +
-                          (size_t)8 * pps * kAttnPage * 2 + (size_t)8 * pages * kAttnPage * 2;
-    if ((int)smem_b > g_rt.max_smem_optin) return false;
+    const size_t smem_a = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 32 * 4 + 8 * D * 2 +
+                          (size_t)8 * pages * kAttnPage * 2;
+    const size_t smem_b = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + (size_t)8 * pps * kAttnPage * 2;
+    if ((int)smem_a > g_rt.max_smem_optin || (int)smem_b > g_rt.max_smem_optin) return false;
     auto ka = attn_split_scores_kernel<T, D>;
     auto kb = attn_split_pv_kernel<T, D>;
     static int conf_a = 0, conf_b = 0;
@@ -698,11 +715,11 @@ bool launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_
     cfg.numAttrs = (pdl && g_rt.pdl) ? 1 : 0;
     cfg.dynamicSmemBytes = smem_a;
     WK_CHECK(cudaLaunchKernelEx(&cfg, ka, q, q_rs, seq_of_row, pos_of_row, kv, G, pps, ws.lpad, scale,
-                                (T *)ws.scores, ws.mpart, g_rt.d_error, early ? 1 : 0));
+                                (T *)ws.scores, ws.mpart, ws.minv, ws.counter_a, g_rt.d_error, early ? 1 : 0));
     cfg.dynamicSmemBytes = smem_b;
     cfg.numAttrs = g_rt.pdl ? 1 : 0;
     WK_CHECK(cudaLaunchKernelEx(&cfg, kb, out, out_rs, seq_of_row, pos_of_row, kv, G, pps, ws.lpad, scale,
-                                (const T *)ws.scores, (const float *)ws.mpart, ws.opart, ws.counter, g_rt.d_error,
+                                (const T *)ws.scores, (const float *)ws.minv, ws.opart, ws.counter, g_rt.d_error,
                                 early ? 1 : 0));
     return true;
 }

@@ -567,7 +567,8 @@ void wk_model_destroy(wk_model *m) {
     void *bufs[] = {m->block_table, m->d_pos, m->d_seq, m->d_ids, m->d_tokens, m->d_row_seq, m->d_row_pos,
                     m->x, m->q, m->att, m->h, m->xn, m->part_val, m->part_key, m->counter,
                     m->p32, m->win_send, m->win_recv, m->d_mk_layers, m->d_mk_maps, m->d_mk_bar,
-                    m->attn_ws.scores, m->attn_ws.mpart, m->attn_ws.opart, m->attn_ws.counter};
+                    m->attn_ws.scores, m->attn_ws.mpart, m->attn_ws.opart, m->attn_ws.counter,
+                    m->attn_ws.minv};
     for (void *p : bufs)
         if (p) cudaFree(p);
     free(m->layers);
@@ -629,8 +630,10 @@ int wk_model_alloc_cache(wk_model *m, int max_batch, int max_ctx) {
         WK_TRY(cudaMallocAsync(&w.scores, rh * 8 * w.lpad * act_size(m->act), s));
         WK_TRY(cudaMallocAsync((void **)&w.mpart, rh * w.max_splits * 8 * sizeof(float), s));
         WK_TRY(cudaMallocAsync((void **)&w.opart, rh * w.max_splits * 8 * c.head_dim * sizeof(float), s));
-        WK_TRY(cudaMallocAsync((void **)&w.counter, rh * sizeof(int), s));
-        WK_TRY(cudaMemsetAsync(w.counter, 0, rh * sizeof(int), s));
+        WK_TRY(cudaMallocAsync((void **)&w.counter, 2 * rh * sizeof(int), s));
+        WK_TRY(cudaMemsetAsync(w.counter, 0, 2 * rh * sizeof(int), s));
+        w.counter_a = w.counter + rh;
+        WK_TRY(cudaMallocAsync((void **)&w.minv, rh * 16 * sizeof(float), s));
     }
     if (m->tp) {
         WK_TRY(cudaMallocAsync(&m->win_send, tp_winner_chunk(max_batch), s));

@@ -94,13 +94,13 @@ __device__ __forceinline__ bool row_valid(const GemvArgs &a, int tile, int r) {
 // that are not 16-byte aligned) a synchronous copy by the warp, zero padded.
 template <int WT>
 __device__ __forceinline__ void issue_unit(const GemvArgs &a, const Smem &sm, int w, int slot, int tile, int chunk,
-                                           int lane, bool tma) {
+                                           int lane, bool tma, int ns) {
     using F = WFmt<WT>;
     const int e0 = chunk * F::kChunk;
-    uint8_t *dst0 = sm.ring + (size_t)(w * kStages + slot) * kStageBytes;
+    uint8_t *dst0 = sm.ring + (size_t)(w * ns + slot) * kStageBytes;
     if (tma) {
         if (lane == 0) {
-            uint64_t *bar = sm.bars + w * kStages + slot;
+            uint64_t *bar = sm.bars + w * ns + slot;
             mbar_expect_tx(bar, kTileRows * F::kRowB);
             const int x = F::chunk_bytes(e0) / 2;  // uint16 column of the box
             if (a.epi == EPI_SWIGLU) {
@@ -128,9 +128,9 @@ __device__ __forceinline__ void issue_unit(const GemvArgs &a, const Smem &sm, in
 template <int WT>
 __device__ __forceinline__ void produce_unit(const GemvArgs &a, const Smem &sm, int w, int slot, int lane,
                                              bool has_work, int ntiles, int nchunks, int &p_tile, int &p_chunk,
-                                             int cstart, int cstep, int tstep) {
+                                             int cstart, int cstep, int tstep, int ns) {
     if (has_work && p_tile < ntiles) {
-        issue_unit<WT>(a, sm, w, slot, p_tile, p_chunk, lane, true);
+        issue_unit<WT>(a, sm, w, slot, p_tile, p_chunk, lane, true, ns);
         p_chunk += cstep;
         if (p_chunk >= nchunks) {
             p_chunk = cstart;
@@ -143,12 +143,12 @@ __device__ __forceinline__ void produce_unit(const GemvArgs &a, const Smem &sm, 
 // two independent accumulators (even / odd slice) to halve the MMA chain.
 template <int WT>
 __device__ __forceinline__ void consume_unit(const GemvArgs &a, const Smem &sm, int w, int slot, int chunk, int lane,
-                                             float (&c)[2][4]) {
+                                             float (&c)[2][4], int ns) {
     using F = WFmt<WT>;
     const int g = lane >> 2, t = lane & 3;
     const int e0 = chunk * F::kChunk;
     const int elems = min(F::kChunk, a.K - e0);
-    const uint8_t *st = sm.ring + (size_t)(w * kStages + slot) * kStageBytes;
+    const uint8_t *st = sm.ring + (size_t)(w * ns + slot) * kStageBytes;
     const uint8_t *r0 = st + g * F::kRowB;
     const uint8_t *r1 = st + (g + 8) * F::kRowB;
     const int M = a.M;
@@ -364,7 +364,7 @@ __device__ __forceinline__ void warp_epilogue(const GemvArgs &a, int tile, int g
     }
 }
 
-template <typename T, int WT>
+template <typename T, int WT, int NS>
 __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
     using F = WFmt<WT>;
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -372,8 +372,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     const int Kpad = nchunks * F::kChunk;
     Smem sm;
     sm.ring = smem_raw;
-    sm.bars = reinterpret_cast<uint64_t *>(sm.ring + (size_t)kWarps * kStages * kStageBytes);
-    sm.xn = reinterpret_cast<uint2 *>(sm.bars + kWarps * kStages);
+    sm.bars = reinterpret_cast<uint64_t *>(sm.ring + (size_t)kWarps * NS * kStageBytes);
+    sm.xn = reinterpret_cast<uint2 *>(sm.bars + kWarps * NS);
     // X goes to shared memory when normalised here, or when small enough
     const bool stage = a.norm_w || (size_t)a.M * Kpad * 2 <= kXStageMax;
     sm.red = reinterpret_cast<float *>(sm.xn + (stage ? (size_t)(Kpad / 4) * a.M : 0));
@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = num_tiles(a);
     const bool tma = a.bulk != 0;
-    if (threadIdx.x < kWarps * kStages) mbar_init(sm.bars + threadIdx.x, 1);
+    if (threadIdx.x < kWarps * NS) mbar_init(sm.bars + threadIdx.x, 1);
     mbar_fence_init();
     __syncthreads();
     if (threadIdx.x == 32 && a.pf) l2_prefetch_slice(a.pf, a.pf_bytes, blockIdx.x, gridDim.x);
@@ -402,8 +402,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     int p_tile = wmode ? gw : (int)blockIdx.x, p_chunk = cstart;  // producer cursor
     const bool has_work = wmode || w < nchunks;  // a warp with no chunk in this K idles in the k-loop
     if (tma)
-        for (int s = 0; s < kStages; ++s)
-            produce_unit<WT>(a, sm, w, s, lane, has_work, ntiles, nchunks, p_tile, p_chunk, cstart, cstep, tstep);
+        for (int s = 0; s < NS; ++s)
+            produce_unit<WT>(a, sm, w, s, lane, has_work, ntiles, nchunks, p_tile, p_chunk, cstart, cstep, tstep, NS);
     // weights are in flight; wait for the producer of X, then let the next kernel
     // in the stream start its own weight prefetch
     pdl_wait();
@@ -423,20 +423,20 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         for (int tile = gw; tile < ntiles; tile += nw) {
             float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
             for (int chunk = 0; chunk < nchunks; ++chunk) {
-                const int slot = consumed % kStages;
+                const int slot = consumed % NS;
                 if (tma) {
-                    if (!mbar_wait_bounded(sm.bars + w * kStages + slot, (consumed / kStages) & 1, a.err, 1))
+                    if (!mbar_wait_bounded(sm.bars + w * NS + slot, (consumed / NS) & 1, a.err, 1))
                         ok = false;
                 } else {
-                    issue_unit<WT>(a, sm, w, slot, tile, chunk, lane, false);
+                    issue_unit<WT>(a, sm, w, slot, tile, chunk, lane, false, NS);
                     __syncwarp();
                 }
-                if (ok) consume_unit<WT>(a, sm, w, slot, chunk, lane, c);
+                if (ok) consume_unit<WT>(a, sm, w, slot, chunk, lane, c, NS);
                 __syncwarp();
                 ++consumed;
                 if (tma && ok)
                     produce_unit<WT>(a, sm, w, slot, lane, has_work, ntiles, nchunks, p_tile, p_chunk, cstart, cstep,
-                                     tstep);
+                                     tstep, NS);
             }
             warp_epilogue<T>(a, tile, g, t, c, bv, bk);
         }
@@ -468,21 +468,21 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         if (has_work) {
             for (int chunk = w; chunk < nchunks; chunk += kWarps) {
-                const int slot = consumed % kStages;
+                const int slot = consumed % NS;
                 if (tma) {
                     // a box that never lands is reported (bounded wait), not waited on forever
-                    if (!mbar_wait_bounded(sm.bars + w * kStages + slot, (consumed / kStages) & 1, a.err, 1))
+                    if (!mbar_wait_bounded(sm.bars + w * NS + slot, (consumed / NS) & 1, a.err, 1))
                         ok = false;
                 } else {
-                    issue_unit<WT>(a, sm, w, slot, tile, chunk, lane, false);
+                    issue_unit<WT>(a, sm, w, slot, tile, chunk, lane, false, NS);
                     __syncwarp();
                 }
-                if (ok) consume_unit<WT>(a, sm, w, slot, chunk, lane, c);
+                if (ok) consume_unit<WT>(a, sm, w, slot, chunk, lane, c, NS);
                 __syncwarp();  // the slot is free again
                 ++consumed;
                 if (tma && ok)
                     produce_unit<WT>(a, sm, w, slot, lane, has_work, ntiles, nchunks, p_tile, p_chunk, cstart, cstep,
-                                     tstep);
+                                     tstep, NS);
             }
         }
         // partial tile of this warp -> shared memory (rows g, g+8; columns 2t, 2t+1)
@@ -552,17 +552,17 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     }
 }
 
-size_t gemv_smem_bytes(int K, int M, int wt, bool norm) {
+size_t gemv_smem_bytes(int K, int M, int wt, bool norm, int ns = kStages) {
     const int chunk = wt == kQ8_0 ? WFmt<kQ8_0>::kChunk : WFmt<kF16>::kChunk;
     const int Kpad = (K + chunk - 1) / chunk * chunk;
     const bool stage = norm || (size_t)M * Kpad * 2 <= kXStageMax;
-    return (size_t)kWarps * kStages * kStageBytes + kWarps * kStages * 8 + (stage ? (size_t)Kpad * M * 2 : 0) +
+    return (size_t)kWarps * ns * kStageBytes + kWarps * ns * 8 + (stage ? (size_t)Kpad * M * 2 : 0) +
            kWarps * 16 * 8 * 4 +
            (8 + 128) * 4 + 128 * 8;
 }
 
-template <typename T, int WT> void launch(const GemvArgs &a, int grid, size_t smem, cudaStream_t s, bool pdl) {
-    auto kern = gemv_kernel<T, WT>;
+template <typename T, int WT, int NS> void launch(const GemvArgs &a, int grid, size_t smem, cudaStream_t s, bool pdl) {
+    auto kern = gemv_kernel<T, WT, NS>;
     // raise the dynamic shared-memory limit only when a launch needs more
     static int configured = 0;
     if ((int)smem > configured) {
@@ -632,17 +632,37 @@ void gemv(GemvArgs a, int act, cudaStream_t s) {
         return;
     }
     const int ntiles = a.epi == EPI_SWIGLU ? (a.F + 7) / 8 : (a.N + kTileRows - 1) / kTileRows;
-    // two CTAs per SM when both fit (about 200 KB of weight tiles in flight per SM)
-    const int per_sm = 2 * (smem + 1024) <= (size_t)g_rt.smem_per_sm ? 2 : 1;
+    // two CTAs per SM when both fit (about 200 KB of weight tiles in flight per
+    // SM); when the 3-stage rings do not fit twice, 2-stage rings that do are
+    // preferred (16 warps per SM hide more latency than deeper rings)
+    size_t smem_used = smem;
+    int ns = kStages;
+    if (2 * (smem + 1024) > (size_t)g_rt.smem_per_sm) {
+        const size_t smem2 = gemv_smem_bytes(a.K, a.M, a.wtype, a.norm_w != nullptr, 2);
+        if (2 * (smem2 + 1024) <= (size_t)g_rt.smem_per_sm) {
+            smem_used = smem2;
+            ns = 2;
+        }
+    }
+    const int per_sm = 2 * (smem_used + 1024) <= (size_t)g_rt.smem_per_sm ? 2 : 1;
     int grid = ntiles < g_rt.num_sms * per_sm ? ntiles : g_rt.num_sms * per_sm;
     if (a.epi == EPI_LOGITS && grid > kMaxLogitCtas) grid = kMaxLogitCtas;
     const bool pdl = g_rt.pdl && a.pdl;
-    if (a.wtype == kQ8_0)
-        launch<__half, kQ8_0>(a, grid, smem, s, pdl);
-    else if (a.wtype == kF16)
-        launch<__half, kF16>(a, grid, smem, s, pdl);
-    else
-        launch<__nv_bfloat16, kBF16>(a, grid, smem, s, pdl);
+    if (ns == 2) {
+        if (a.wtype == kQ8_0)
+            launch<__half, kQ8_0, 2>(a, grid, smem_used, s, pdl);
+        else if (a.wtype == kF16)
+            launch<__half, kF16, 2>(a, grid, smem_used, s, pdl);
+        else
+            launch<__nv_bfloat16, kBF16, 2>(a, grid, smem_used, s, pdl);
+    } else {
+        if (a.wtype == kQ8_0)
+            launch<__half, kQ8_0, kStages>(a, grid, smem_used, s, pdl);
+        else if (a.wtype == kF16)
+            launch<__half, kF16, kStages>(a, grid, smem_used, s, pdl);
+        else
+            launch<__nv_bfloat16, kBF16, kStages>(a, grid, smem_used, s, pdl);
+    }
 }
 
 }  // namespace wk

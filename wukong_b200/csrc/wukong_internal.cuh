@@ -134,7 +134,9 @@ struct AttnSplitWs {
     void *scores = nullptr;     // [max_rows][max_kv_heads][8][lpad] (type T)
     float *mpart = nullptr;     // [max_rows][max_kv_heads][max_splits][8]
     float *opart = nullptr;     // [max_rows][max_kv_heads][max_splits][8][head_dim]
-    int *counter = nullptr;     // [max_rows][max_kv_heads], zero between launches
+    int *counter = nullptr;     // [max_rows][max_kv_heads], zero between launches (P.V launch)
+    int *counter_a = nullptr;   // the same for the scores launch
+    float *minv = nullptr;      // [max_rows][max_kv_heads][8][2] row max and 1 / softmax sum per head
     int max_rows = 0, max_kv_heads = 0, max_splits = 0, lpad = 0;
 };
 // Returns the number of kernel launches.
