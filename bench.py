@@ -140,8 +140,9 @@ def run_ours(args, rank, world, local_rank):
         torch.distributed.broadcast(t, 0)
         wk.check(L.wk_tp_init(rank, world, bytes(t.cpu().numpy())))
     B, K, W, P = args.batch, args.steps, args.warmup, args.prompt
-    ctx = P + W + K + 8
     e2e_abi = not args.no_e2e and tpw == 1
+    # the engine e2e leg (tensor-parallel runs) continues decoding after the timed steps
+    ctx = P + W + K + 8 + (W + K if (not args.no_e2e and not e2e_abi) else 0)
     sm = SyntheticLlama(cfg, ctx, seed=SEED, unfused=e2e_abi, tp_rank=rank if tpw > 1 else 0, tp_world=tpw)
     eng = Engine.from_synthetic(sm, max_batch=B, tp=tpw > 1)
     prompt = np.random.default_rng(7).integers(0, cfg["V"], size=(B, P)).astype(np.int32)
@@ -250,6 +251,7 @@ def run_e2e_engine(L, eng, B, K, W, world):
     """The engine with host I/O every step: the step's ids are copied from
     pinned host memory, the step runs, its tokens are read back."""
     import torch
+    import wukong_b200 as wk
     ids = torch.zeros(B, dtype=torch.int32).pin_memory()
     toks = torch.zeros(B, dtype=torch.int32).pin_memory()
     nxt = L.wk_model_next_ids(eng.m)
@@ -257,7 +259,7 @@ def run_e2e_engine(L, eng, B, K, W, world):
 
     def step():
         L.cuda_to_device(nxt, ctypes.c_void_p(ids.data_ptr()), 4 * B)
-        L.wk_model_decode_step(eng.m)
+        wk.check(L.wk_model_decode_step(eng.m))
         L.cuda_to_host(ctypes.c_void_p(toks.data_ptr()), cur, 4 * B)
         ids.copy_(toks)
 
