@@ -7,19 +7,21 @@
 // exactly as the reference does (w = (half)(float(scale) * q)), multiplied with
 // half activations, accumulated in fp32 and rounded once to half at the store.
 //
-// CTA = 6 warps, one output tile per CTA:
+// CTA = 10 warps, one output tile per CTA:
 //   warp 0 (lane 0)  TMA producer: raw Q8_0 tiles (128 rows x 256 k = 128 x 272 B,
 //                    one 2-D box) and activation tiles (BN rows x 64 k, 128-byte
 //                    swizzle); for 16-bit weights also the A tiles.
 //   warp 1           allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN,
 //                    K=16 per instruction) and tcgen05.commit.
-//   warps 2..5       one thread per weight row: read the raw row from shared
-//                    memory (conflict-free 16-byte loads), dequantise in registers
-//                    (byte-permute -> exact half2, half2 multiply by the scale) and
-//                    write the 128-byte-swizzled fp16 A tile the UMMA descriptor
-//                    expects; after the K loop they drain TMEM (tcgen05.ld) and run
-//                    the fused epilogue (store+bias, residual, RoPE+KV append,
-//                    SwiGLU pairing of up/gate rows).
+//   warps 2..9       two threads per weight row (warps 2..5 Q8_0 blocks 0..3 of
+//                    each 256-k raw stage, warps 6..9 blocks 4..7): read the raw
+//                    bytes from shared memory (16-byte loads), dequantise in
+//                    registers (byte-permute -> exact half2, half2 multiply by the
+//                    scale) and write the 128-byte-swizzled fp16 A tile the UMMA
+//                    descriptor expects; after the K loop warps 2..5 drain TMEM
+//                    (tcgen05.ld) and run the fused epilogue (store+bias,
+//                    residual, RoPE+KV append, SwiGLU pairing of up/gate rows).
+// The operand ring holds 4 stages for 128-token tiles and 6 for 64 / 32.
 // Every mbarrier wait is bounded (one second); a wait that gives up records an
 // error code and the CTA runs to completion without further waiting.
 #include <cudaTypedefs.h>
@@ -31,8 +33,12 @@ namespace wk {
 
 namespace {
 
-constexpr int kThreads = 192;
-constexpr int kASlots = 4;                      // 64-k operand stages
+constexpr int kThreads = 320;
+constexpr int kMaxSlots = 6;                    // 64-k operand stages (deepest ring)
+// operand ring depth: 4 stages of 128-token B tiles fit beside the raw ring, 6 of 64 / 32
+template <int BN> struct Slots {
+    static constexpr int n = BN >= 128 ? 4 : 6;
+};
 constexpr int kRawSlots = 2;                    // 256-k raw Q8_0 stages
 constexpr int kATileBytes = 128 * 128;          // 128 rows x 64 halves
 constexpr int kRawBytes = 128 * 272;            // 128 rows x 8 Q8_0 blocks
@@ -96,7 +102,7 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 
 struct Bars {
     uint64_t raw_full[kRawSlots], raw_empty[kRawSlots];
-    uint64_t a_full[kASlots], b_full[kASlots], ab_empty[kASlots];
+    uint64_t a_full[kMaxSlots], b_full[kMaxSlots], ab_empty[kMaxSlots];
     uint64_t acc_full;
     uint32_t tmem;
 };
@@ -104,21 +110,22 @@ struct Bars {
 template <int BN> struct Layout {
     static constexpr int kBTile = BN * 128;
     static constexpr size_t kA = 0;
-    static constexpr size_t kB = kA + (size_t)kASlots * kATileBytes;
-    static constexpr size_t kRaw = kB + (size_t)kASlots * kBTile;
+    static constexpr size_t kB = kA + (size_t)Slots<BN>::n * kATileBytes;
+    static constexpr size_t kRaw = kB + (size_t)Slots<BN>::n * kBTile;
     static constexpr size_t kBars = kRaw + (size_t)kRawSlots * kRawBytes;
     static constexpr size_t kTotal = kBars + sizeof(Bars) + 1024;  // + alignment slack
 };
 
-// Dequantise 64 k (Q8_0 blocks 2j, 2j+1 of this row's 272 raw bytes held in
-// `w`, 68 words) into the 128-byte swizzled A row.
-__device__ __forceinline__ void dequant_sub(const uint32_t (&w)[68], int j, uint8_t *arow, int row) {
+// Dequantise 64 k (Q8_0 blocks 2j, 2j+1 of this row's 272 raw bytes; `w` holds
+// the row's bytes [BASE, BASE + 4 NW)) into the 128-byte swizzled A row.
+template <int BASE, int NW>
+__device__ __forceinline__ void dequant_sub(const uint32_t (&w)[NW], int j, uint8_t *arow, int row) {
 #pragma unroll
     for (int bb = 0; bb < 2; ++bb) {
         const int b = 2 * j + bb;  // compile-time after unrolling j
         const int off = 34 * b;    // byte offset of the block
         // scale: bytes off, off+1
-        const uint32_t sw = w[off >> 2];
+        const uint32_t sw = w[(off - BASE) >> 2];
         const uint32_t sbits = (off & 2) ? (sw >> 16) : (sw & 0xffffu);
         const __half2 s2 = __half2half2(__ushort_as_half((unsigned short)sbits));
         // 32 quants start at off + 2: 8 words, realigned when off + 2 is not 4-aligned
@@ -127,9 +134,9 @@ __device__ __forceinline__ void dequant_sub(const uint32_t (&w)[68], int j, uint
         for (int i = 0; i < 8; ++i) {
             const int byte = off + 2 + 4 * i;
             if (byte & 2)
-                q[i] = __byte_perm(w[byte >> 2], w[(byte >> 2) + 1], 0x5432);
+                q[i] = __byte_perm(w[(byte - BASE) >> 2], w[((byte - BASE) >> 2) + 1], 0x5432);
             else
-                q[i] = w[byte >> 2];
+                q[i] = w[(byte - BASE) >> 2];
         }
         // 32 halves = 4 x 16-byte chunks (chunk c covers k = 8c .. 8c+7 of the 64-k sub-tile)
 #pragma unroll
@@ -207,6 +214,7 @@ __device__ __forceinline__ void store_out(const GemmArgs &a, int n, int m, float
 template <typename T, int WT, int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
     using L = Layout<BN>;
+    constexpr int kASlots = Slots<BN>::n;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -227,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     if (threadIdx.x == 0) {
         for (int i = 0; i < kRawSlots; ++i) {
             mbar_init(&bars->raw_full[i], 1);
-            mbar_init(&bars->raw_empty[i], 128);
+            mbar_init(&bars->raw_empty[i], 256);  // every dequantising thread
         }
         for (int i = 0; i < kASlots; ++i) {
             mbar_init(&bars->a_full[i], kQ8 ? 128 : 1);
@@ -314,8 +322,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         }
         pdl_trigger();
     } else {
-        // warps 2..5: row = TMEM lane quarter (warp % 4) * 32 + lane
+        // warps 2..9 dequantise: row = (warp % 4) * 32 + lane (the TMEM lane quarter
+        // of warps 2..5, which also run the epilogue); warps 2..5 take Q8_0 blocks
+        // 0..3 of each 256-k raw stage (A sub-tiles 0, 1), warps 6..9 blocks 4..7
         const int row = (warp & 3) * 32 + lane;
+        const int half = (warp - 2) >> 2;
         pdl_trigger();
         if (kQ8) {
             for (int kb = 0; kb < nkb && ok; ++kb) {
@@ -324,31 +335,39 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                     ok = false;
                     break;
                 }
-                uint32_t w[68];
-                const uint4 *src = reinterpret_cast<const uint4 *>(RAW + (size_t)rs * kRawBytes + row * 272);
+                // bytes [128 half, 128 half + 144) of the row: blocks 4 half .. 4 half + 3
+                uint32_t w[36];
+                const uint4 *src =
+                    reinterpret_cast<const uint4 *>(RAW + (size_t)rs * kRawBytes + row * 272 + half * 128);
 #pragma unroll
-                for (int i = 0; i < 17; ++i) {
+                for (int i = 0; i < 9; ++i) {
                     const uint4 v = src[i];
                     w[4 * i] = v.x;
                     w[4 * i + 1] = v.y;
                     w[4 * i + 2] = v.z;
                     w[4 * i + 3] = v.w;
                 }
-                mbar_arrive(&bars->raw_empty[rs]);  // the raw row is in registers
+                mbar_arrive(&bars->raw_empty[rs]);  // this part of the raw row is in registers
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
+                for (int jj = 0; jj < 2; ++jj) {
+                    const int j = 2 * half + jj;
                     const int i = kb * 4 + j;
                     const int s = i % kASlots;
                     if (i >= kASlots && !mbar_wait_bounded(&bars->ab_empty[s], ((i / kASlots) - 1) & 1, err, 15)) {
                         ok = false;
                         break;
                     }
-                    dequant_sub(w, j, A + (size_t)s * kATileBytes + row * 128, row);
+                    uint8_t *arow = A + (size_t)s * kATileBytes + row * 128;
+                    if (half == 0)
+                        dequant_sub<0>(w, jj, arow, row);
+                    else
+                        dequant_sub<128>(w, 2 + jj, arow, row);
                     fence_proxy_async();  // generic-proxy writes -> visible to tcgen05.mma
                     mbar_arrive(&bars->a_full[s]);
                 }
             }
         }
+        if (half == 0) {
         // epilogue: TMEM -> registers -> fused store (reads residual / positions
         // written by earlier kernels)
         pdl_wait();
@@ -380,6 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 if (row_ok && m < a.M) store_out<T>(a, n, m, __uint_as_float(v[i]), &pv);
             }
         }
+        }  // half == 0: the epilogue warps
     }
     tc_fence_before();
     __syncthreads();
@@ -430,7 +450,8 @@ void gemm_tc(GemmArgs a, int act, cudaStream_t s) {
     if (!a.err) a.err = g_rt.d_error;
     const size_t es = 2;
     // activations: [M rows][K] with row stride ldx, boxes of 64 k x BN rows, 128-byte swizzle
-    const int BN = a.M >= 96 ? 128 : (a.M >= 48 ? 64 : 32);
+    // token tile: 128 only for long blocks; 64 for M >= 48 so that M = 128 spreads over twice the CTAs
+    const int BN = a.M >= 256 ? 128 : (a.M >= 48 ? 64 : 32);
     if (((uintptr_t)a.x % 16) || ((a.ldx * es) % 16)) WK_PANIC("gemm_tc: activations must be 16-byte aligned rows");
     if (!encode_map_2d(&a.xmap, a.x, act == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                        (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.ldx * es, 64, (uint32_t)BN,

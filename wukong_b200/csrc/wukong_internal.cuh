@@ -108,7 +108,8 @@ struct GemmArgs {
 };
 bool gemm_tc_supported(int wtype, int act, int K, int N, int epi, int F);
 void gemm_tc(GemmArgs a, int act, cudaStream_t s);
-// Minimum activation rows for which the tcgen05 GEMM replaces the GEMV.
+// Minimum activation rows for which the tcgen05 GEMM replaces the GEMV
+// (measured, 8192 x 2048 Q8_0, M = 16: 19.6 us on tcgen05, 24.3 us as two 8-row GEMV passes).
 constexpr int kTcMinRows = 16;
 
 // ---------------------------------------------------------------- ops.cu
