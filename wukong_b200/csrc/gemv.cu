@@ -205,14 +205,25 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 
 // RMSNorm prologue: normalise X, rounded to T as the reference stores its
 // rmsnorm output (cuda.cu:533-601), into shared memory [M][Kpad] (zero padded).
+// The rows are copied in with 8-byte loads first (one round trip instead of a
+// dependent load per element), then summed from shared memory in the same
+// order (lane l adds elements l, l + 32, ...) and normalised in place.
 template <typename T>
 __device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad) {
     const int M = a.M;
     const T *x = reinterpret_cast<const T *>(a.x);
+    const int nq = Kpad / 4;
+    for (int i = threadIdx.x; i < nq * M; i += blockDim.x) {
+        const int m = i / nq, k = (i - m * nq) * 4;
+        sm.xn[i] = k < a.K ? *reinterpret_cast<const uint2 *>(x + (long)m * a.ldx + k) : make_uint2(0u, 0u);
+    }
+    __syncthreads();
+    if (!a.norm_w) return;
+    const T *xs = reinterpret_cast<const T *>(sm.xn);
     // one warp per activation row: sum of squares
     const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int m = wid; a.norm_w && m < M; m += kWarps) {
-        const T *xr = x + (long)m * a.ldx;
+    for (int m = wid; m < M; m += kWarps) {
+        const T *xr = xs + (long)m * Kpad;
         float ss = 0.f;
         for (int k = lane; k < a.K; k += 32) {
             float v = to_float(xr[k]);
@@ -222,21 +233,18 @@ __device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad) {
         if (lane == 0) sm.misc[m] = rsqrtf(ss / (float)a.K + a.eps);
     }
     __syncthreads();
-    const int nq = Kpad / 4;
     for (int i = threadIdx.x; i < nq * M; i += blockDim.x) {
-        const int m = i / nq, kq = i - m * nq;
-        const int k = kq * 4;
-        const T *xr = x + (long)m * a.ldx;
+        const int m = i / nq, k = (i - m * nq) * 4;
+        if (k >= a.K) continue;  // the zero padding stays zero
+        const uint2 r = sm.xn[i];
+        const T *rv = reinterpret_cast<const T *>(&r);
         float v[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-            v[j] = (k + j < a.K) ? (a.norm_w ? (to_float(xr[k + j]) * sm.misc[m]) * a.norm_w[k + j]
-                                             : to_float(xr[k + j]))
-                                 : 0.f;
+        for (int j = 0; j < 4; ++j) v[j] = (to_float(rv[j]) * sm.misc[m]) * a.norm_w[k + j];
         uint2 pk;
         pk.x = pack2<T>(v[0], v[1]);
         pk.y = pack2<T>(v[2], v[3]);
-        sm.xn[(long)m * nq + kq] = pk;
+        sm.xn[i] = pk;
     }
 }
 
