@@ -225,15 +225,20 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     const int Lpad = npages * kAttnPage;
     const T *K = reinterpret_cast<const T *>(kv.k);
     const T *V = reinterpret_cast<const T *>(kv.v);
+    // the sequence's page ids, read once (one round trip, not one per page copy)
+    int *pgs = reinterpret_cast<int *>(sc + 8 * Lpad_max);
+    const int *bt = kv.block_table + (long)seq * kv.max_pages;
     auto page_src = [&](int i) -> const T * {
         // units 0..npages-1 are K pages, npages..2*npages-1 the V pages
         const int p = i < npages ? i : i - npages;
-        const long pg = kv.block_table[(long)seq * kv.max_pages + p];
-        return (i < npages ? K : V) + (pg * kv.kv_heads + kvh) * (long)kAttnPage * D;
+        return (i < npages ? K : V) + ((long)pgs[p] * kv.kv_heads + kvh) * (long)kAttnPage * D;
     };
     if (tid == 64 && pf)
         l2_prefetch_slice(pf, pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     if (tid < kAttnSlots) mbar_init(bars + tid, 1);
+    // decode: the block table is not written by the producing kernel
+    if (early)
+        for (int i = tid; i < npages; i += 128) pgs[i] = bt[i];
     mbar_fence_init();
     __syncthreads();
     const int total = 2 * npages;
@@ -247,9 +252,21 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
             mbar_expect_tx(bars + issued, kPageBytes);
             bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
         }
+        // the other complete pages (K past the ring, all V but the newest) go to L2
+        for (int p = issued; p < npages - 1; ++p)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(page_src(p)), "r"((uint32_t)kPageBytes)
+                         : "memory");
+        for (int p = 0; p < npages - 1; ++p)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(page_src(npages + p)),
+                         "r"((uint32_t)kPageBytes)
+                         : "memory");
     }
     pdl_wait();
     pdl_trigger();
+    if (!early) {
+        for (int i = tid; i < npages; i += 128) pgs[i] = bt[i];
+        __syncthreads();
+    }
     if (tid == 0) {
         for (; issued < kAttnSlots && issued < total; ++issued) {
             mbar_expect_tx(bars + issued, kPageBytes);
@@ -318,20 +335,42 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     // ---- softmax numerators: thread -> (head h, keys j = i, i + 16, ...)
     const int h = tid >> 4, i0 = tid & 15;  // 8 heads x 16 threads
     const float M = fmaxf(fmaxf(red[h * 4], red[h * 4 + 1]), fmaxf(red[h * 4 + 2], red[h * 4 + 3]));
+    // keys j = i0 + 16 u; eight at a time so that the loads and exponentials
+    // overlap, summed in ascending j as one at a time would
+    T *srow = sc + h * Lpad_max;
     float lsum = 0.f;
-    for (int j = i0; j < Lpad; j += 16) {
-        float e = 0.f;
-        if (j < L && h < G) {
-            e = expf(to_float(sc[h * Lpad_max + j]) * scale - M);
-            lsum += e;
+    for (int j0 = i0; j0 < Lpad; j0 += 16 * 8) {
+        float e[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = j0 + 16 * u;
+            e[u] = j < L && h < G ? to_float(srow[j]) : 0.f;
         }
-        sc[h * Lpad_max + j] = from_float<T>(e);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = j0 + 16 * u;
+            if (j < L && h < G) {
+                e[u] = expf(e[u] * scale - M);
+                lsum += e[u];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (j0 + 16 * u < Lpad) srow[j0 + 16 * u] = from_float<T>(e[u]);
     }
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
     const float inv = 1.0f / lsum;
-    for (int j = i0; j < L; j += 16)
-        if (h < G) sc[h * Lpad_max + j] = from_float<T>(to_float(sc[h * Lpad_max + j]) * inv);
+    if (h < G)
+        for (int j0 = i0; j0 < L; j0 += 16 * 8) {
+            float e[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (j0 + 16 * u < L) e[u] = to_float(srow[j0 + 16 * u]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (j0 + 16 * u < L) srow[j0 + 16 * u] = from_float<T>(e[u] * inv);
+        }
     __syncthreads();
 
     // ---- pass 2: O^T = V^T . P^T; warp w owns d-tiles w, w + 4
@@ -425,8 +464,12 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
     const int p0 = z * pps, p1 = min(p0 + pps, npages);
     const int n = p1 > p0 ? p1 - p0 : 0;
     const T *K = reinterpret_cast<const T *>(kv.k);
+    // decode: the newest page's id is read before the wait too (the block
+    // table is not written by the producing kernel)
+    const int *bt = kv.block_table + (long)seq * kv.max_pages;
+    const long pg_last = early && tid == 0 && n > 0 && p1 == npages ? bt[npages - 1] : -1;
     auto page_src = [&](int i) -> const T * {
-        const long pg = kv.block_table[(long)seq * kv.max_pages + p0 + i];
+        const long pg = pg_last >= 0 && p0 + i == npages - 1 ? pg_last : bt[p0 + i];
         return K + (pg * kv.kv_heads + kvh) * (long)kAttnPage * D;
     };
     if (tid < kAttnSlots) mbar_init(bars + tid, 1);
@@ -567,8 +610,12 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
     const int n = p1 > p0 ? p1 - p0 : 0;
     const int wl = pps * kAttnPage;  // row length of pl
     const T *V = reinterpret_cast<const T *>(kv.v);
+    // decode: the newest page's id is read before the wait too (the block
+    // table is not written by the producing kernel)
+    const int *bt = kv.block_table + (long)seq * kv.max_pages;
+    const long pg_last = early && tid == 0 && n > 0 && p1 == npages ? bt[npages - 1] : -1;
     auto page_src = [&](int i) -> const T * {
-        const long pg = kv.block_table[(long)seq * kv.max_pages + p0 + i];
+        const long pg = pg_last >= 0 && p0 + i == npages - 1 ? pg_last : bt[p0 + i];
         return V + (pg * kv.kv_heads + kvh) * (long)kAttnPage * D;
     };
     if (tid < kAttnSlots) mbar_init(bars + tid, 1);
@@ -730,7 +777,7 @@ void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq
                       long pf_bytes, bool early) {
     const int Lpad = (max_len + kAttnPage - 1) / kAttnPage * kAttnPage;
     const size_t smem = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 64 * 4 + 8 * D * 2 +
-                        (size_t)8 * Lpad * 2;
+                        (size_t)8 * Lpad * 2 + (size_t)(Lpad / kAttnPage) * 4;
     if ((int)smem > g_rt.max_smem_optin) WK_PANIC("attention: context %d needs %zu B of shared memory", max_len, smem);
     auto kern = attn_decode_tc_kernel<T, D>;
     static int configured = 0;

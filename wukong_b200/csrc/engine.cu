@@ -257,6 +257,12 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
         return wt == kQ8_0 ? rows * (K / 32) * 34 : rows * (long)K * 2;
     };
     const int W = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+    // Below kTcMinRows every linear layer here runs on the GEMV, so the launch
+    // before each GEMV is a GEMV, an attention kernel (both trigger their
+    // dependents after their own wait) or a plain launch: what the launch
+    // before that wrote is complete when the GEMV starts, and the GEMV may read
+    // its side inputs before its wait
+    const int pre = rows < kTcMinRows;
     const long logit_bytes = wbytes(c.vocab, d, c.out_wtype);
     const long logit_pf = logit_bytes < (48L << 20) ? logit_bytes : (48L << 20);
     for (int l = 0; l < c.n_layers; ++l) {
@@ -289,6 +295,7 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.max_pages = kv.max_pages;
             a.page = kPage;
             a.kv_heads = c.n_kv_heads;
+            a.pre = pre;
             a.pf = L.o;
             a.pf_bytes = wbytes(d, col, c.wtype);
             launches += linear(a, rows, m->act, s, m->xn);
@@ -322,6 +329,7 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
                 a.ldo = d;
                 a.res = m->x;
                 a.ldr = d;
+                a.pre = pre;
             }
             a.pf = L.fc;
             a.pf_bytes = wbytes(2L * c.ffn, d, c.wtype) / 2;
@@ -364,6 +372,7 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
                 a.ldo = d;
                 a.res = m->x;
                 a.ldr = d;
+                a.pre = pre;
             }
             a.pf = last ? (const void *)m->out_w : (const void *)m->layers[l + 1].qkv;
             a.pf_bytes = last ? logit_pf : wbytes(W, d, c.wtype);

@@ -203,19 +203,63 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     return (uint32_t)*reinterpret_cast<uint16_t *>(&ha) | ((uint32_t)*reinterpret_cast<uint16_t *>(&hb) << 16);
 }
 
+// RMSNorm weights held in registers from before griddepcontrol.wait (they do
+// not depend on the previous kernel): thread t takes k = 4 (t + 256 j), j < 4,
+// which covers K <= 4096; larger K loads the rest after the wait.
+constexpr int kNormRegs = 4;
+struct NormW {
+    float4 v[kNormRegs];
+};
+__device__ __forceinline__ float4 load_norm4(const float *w, int k) {
+    if ((reinterpret_cast<uintptr_t>(w) & 15) == 0) return *reinterpret_cast<const float4 *>(w + k);
+    return make_float4(w[k], w[k + 1], w[k + 2], w[k + 3]);
+}
+__device__ __forceinline__ void norm_pre(const GemvArgs &a, NormW &nw) {
+#pragma unroll
+    for (int j = 0; j < kNormRegs; ++j) {
+        const int k = (threadIdx.x + j * blockDim.x) * 4;
+        nw.v[j] = k < a.K ? load_norm4(a.norm_w, k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
 // RMSNorm prologue: normalise X, rounded to T as the reference stores its
 // rmsnorm output (cuda.cu:533-601), into shared memory [M][Kpad] (zero padded).
 // The rows are copied in with 8-byte loads first (one round trip instead of a
 // dependent load per element), then summed from shared memory in the same
 // order (lane l adds elements l, l + 32, ...) and normalised in place.
 template <typename T>
-__device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad) {
+__device__ __forceinline__ void norm_quad(const GemvArgs &a, const Smem &sm, int nq, int kq, float4 w) {
+    for (int m = 0; m < a.M; ++m) {
+        const int i = m * nq + kq;
+        const uint2 r = sm.xn[i];
+        const T *rv = reinterpret_cast<const T *>(&r);
+        const float wv[4] = {w.x, w.y, w.z, w.w};
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = (to_float(rv[j]) * sm.misc[m]) * wv[j];
+        uint2 pk;
+        pk.x = pack2<T>(v[0], v[1]);
+        pk.y = pack2<T>(v[2], v[3]);
+        sm.xn[i] = pk;
+    }
+}
+template <typename T>
+__device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad, const NormW &nw) {
     const int M = a.M;
     const T *x = reinterpret_cast<const T *>(a.x);
-    const int nq = Kpad / 4;
-    for (int i = threadIdx.x; i < nq * M; i += blockDim.x) {
+    const int nq = Kpad / 4, total = nq * M, nt = blockDim.x;
+    auto ld = [&](int i) -> uint2 {
         const int m = i / nq, k = (i - m * nq) * 4;
-        sm.xn[i] = k < a.K ? *reinterpret_cast<const uint2 *>(x + (long)m * a.ldx + k) : make_uint2(0u, 0u);
+        return k < a.K ? *reinterpret_cast<const uint2 *>(x + (long)m * a.ldx + k) : make_uint2(0u, 0u);
+    };
+    for (int i = threadIdx.x; i < total; i += 8 * nt) {  // up to 8 loads in flight per thread
+        uint2 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (i + j * nt < total) v[j] = ld(i + j * nt);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (i + j * nt < total) sm.xn[i + j * nt] = v[j];
     }
     __syncthreads();
     if (!a.norm_w) return;
@@ -233,19 +277,14 @@ __device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad) {
         if (lane == 0) sm.misc[m] = rsqrtf(ss / (float)a.K + a.eps);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < nq * M; i += blockDim.x) {
-        const int m = i / nq, k = (i - m * nq) * 4;
-        if (k >= a.K) continue;  // the zero padding stays zero
-        const uint2 r = sm.xn[i];
-        const T *rv = reinterpret_cast<const T *>(&r);
-        float v[4];
+    // normalise in place; the zero padding (k >= K) stays zero
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = (to_float(rv[j]) * sm.misc[m]) * a.norm_w[k + j];
-        uint2 pk;
-        pk.x = pack2<T>(v[0], v[1]);
-        pk.y = pack2<T>(v[2], v[3]);
-        sm.xn[i] = pk;
+    for (int j = 0; j < kNormRegs; ++j) {
+        const int kq = threadIdx.x + j * blockDim.x;
+        if (kq * 4 < a.K) norm_quad<T>(a, sm, nq, kq, nw.v[j]);
     }
+    for (int kq = threadIdx.x + kNormRegs * blockDim.x; kq * 4 < a.K; kq += blockDim.x)
+        norm_quad<T>(a, sm, nq, kq, load_norm4(a.norm_w, kq * 4));
 }
 
 // Threads 0..127 own one (row r, column m) output of the 16 x 8 tile; `red`
@@ -259,13 +298,47 @@ __device__ __forceinline__ float tile_sum(const float *red, int r, int m) {
     return acc;
 }
 
+// Inputs of the epilogue other than the tile itself, for output row n and
+// activation row m: the residual (RESID); the RoPE (cos, sin) pair at the
+// row's position and the K/V cache offset of its token (QKV).
+struct Side {
+    float s0 = 0.f, s1 = 0.f;
+    long off = 0;
+};
+__device__ __forceinline__ bool has_side(int epi) { return epi == EPI_RESID || epi == EPI_QKV; }
 template <typename T>
-__device__ void epilogue(const GemvArgs &a, const float *red, int tile, float &best_v, uint64_t &best_k) {
+__device__ __forceinline__ Side side_inputs(const GemvArgs &a, int n, int m) {
+    Side s;
+    if (a.epi == EPI_RESID) {
+        s.s0 = to_float(reinterpret_cast<const T *>(a.res)[(long)m * a.ldr + n]);
+    } else if (a.epi == EPI_QKV) {
+        const int pos = a.pos[m];
+        const bool rope = n < a.nq + a.nk;
+        const int base = n < a.nq ? 0 : (rope ? a.nq : a.nq + a.nk);
+        const int dd = (n - base) % a.hd;
+        if (rope) {
+            const float *f = a.freqs + (long)pos * a.hd + (dd & ~1);
+            s.s0 = f[0];
+            s.s1 = f[1];
+        }
+        if (n >= a.nq) {
+            const long page = a.block_table[(long)a.seq[m] * a.max_pages + pos / a.page];
+            s.off = ((page * a.kv_heads + (n - base) / a.hd) * a.page + pos % a.page) * a.hd + dd;
+        }
+    }
+    return s;
+}
+
+// pre: the side inputs of this thread's (row, column), read before the wait
+template <typename T>
+__device__ void epilogue(const GemvArgs &a, const float *red, int tile, float &best_v, uint64_t &best_k,
+                         const Side *pre) {
     const int tid = threadIdx.x;
     const int r = (tid >> 3) & 15, m = tid & 7;
     if (tid >= 128 || m >= a.M || !row_valid(a, tile, r)) return;
-    float acc = tile_sum(red, r, m);
     const int n = tile_row(a, tile, r);
+    const Side sd = pre ? *pre : has_side(a.epi) ? side_inputs<T>(a, n, m) : Side();
+    float acc = tile_sum(red, r, m);
     switch (a.epi) {
     case EPI_STORE: {
         if (a.bias) acc += to_float(reinterpret_cast<const T *>(a.bias)[n]);
@@ -274,32 +347,21 @@ __device__ void epilogue(const GemvArgs &a, const float *red, int tile, float &b
     }
     case EPI_RESID: {
         const float y = round_to<T>(acc);
-        const float rv = to_float(reinterpret_cast<const T *>(a.res)[(long)m * a.ldr + n]);
-        reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(rv + y);
+        reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(sd.s0 + y);
         break;
     }
     case EPI_QKV: {
         const float y = round_to<T>(acc);
-        const int pos = a.pos[m];
         if (n < a.nq + a.nk) {
             const float yp = round_to<T>(tile_sum(red, r ^ 1, m));
-            const int dd = (n - (n < a.nq ? 0 : a.nq)) % a.hd;
-            const float *f = a.freqs + (long)pos * a.hd + (dd & ~1);
-            const float cs = f[0], sn = f[1];
+            const float cs = sd.s0, sn = sd.s1;
             const float o = (n & 1) ? (yp * sn + y * cs) : (y * cs - yp * sn);
-            if (n < a.nq) {
+            if (n < a.nq)
                 reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(o);
-            } else {
-                const int kh = (n - a.nq) / a.hd;
-                const long page = a.block_table[(long)a.seq[m] * a.max_pages + pos / a.page];
-                const long off = ((page * a.kv_heads + kh) * a.page + pos % a.page) * a.hd + dd;
-                reinterpret_cast<T *>(a.kpool)[off] = from_float<T>(o);
-            }
+            else
+                reinterpret_cast<T *>(a.kpool)[sd.off] = from_float<T>(o);
         } else {
-            const int dd = (n - a.nq - a.nk) % a.hd, vh = (n - a.nq - a.nk) / a.hd;
-            const long page = a.block_table[(long)a.seq[m] * a.max_pages + pos / a.page];
-            const long off = ((page * a.kv_heads + vh) * a.page + pos % a.page) * a.hd + dd;
-            reinterpret_cast<T *>(a.vpool)[off] = from_float<T>(y);
+            reinterpret_cast<T *>(a.vpool)[sd.off] = from_float<T>(y);
         }
         break;
     }
@@ -412,11 +474,23 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     if (tma)
         for (int s = 0; s < NS; ++s)
             produce_unit<WT>(a, sm, w, s, lane, has_work, ntiles, nchunks, p_tile, p_chunk, cstart, cstep, tstep, NS);
+    // Inputs that the previous kernel does not write are read before the wait:
+    // the RMSNorm weights, and with a.pre the side inputs of this CTA's first
+    // tile (written two or more launches back).
+    NormW normw;
+    if (stage && a.norm_w) norm_pre(a, normw);
+    Side side0;
+    const bool pre = a.pre && !wmode && has_side(a.epi) && (int)blockIdx.x < ntiles;
+    if (pre) {
+        const int r = (threadIdx.x >> 3) & 15, m = threadIdx.x & 7;
+        if (threadIdx.x < 128 && m < a.M && row_valid(a, blockIdx.x, r))
+            side0 = side_inputs<T>(a, tile_row(a, blockIdx.x, r), m);
+    }
     // weights are in flight; wait for the producer of X, then let the next kernel
     // in the stream start its own weight prefetch
     pdl_wait();
     pdl_trigger();
-    if (stage) stage_xn<T>(a, sm, Kpad);
+    if (stage) stage_xn<T>(a, sm, Kpad, normw);
     __syncthreads();
 
     float best_v = -INFINITY;
@@ -501,7 +575,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         red[(g + 8) * 8 + 2 * t] = c[0][2] + c[1][2];
         red[(g + 8) * 8 + 2 * t + 1] = c[0][3] + c[1][3];
         __syncthreads();
-        epilogue<T>(a, sm.red, tile, best_v, best_k);
+        epilogue<T>(a, sm.red, tile, best_v, best_k, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
         __syncthreads();  // red is rewritten by the next tile
     }
 

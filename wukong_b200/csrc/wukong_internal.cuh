@@ -63,6 +63,11 @@ struct GemvArgs {
     int bulk = 1;  // set by gemv(): 1 when the weight tiles stream by TMA
     int pdl = 1;   // launch with programmatic dependent launch
     int warp_tile_min = 1 << 30;  // set by gemv() from g_rt.warp_tile_min
+    // 1: the epilogue's side inputs (residual; positions, block table and RoPE
+    // table) were written two or more launches earlier in a stream whose kernels
+    // all let their dependents start only after their own griddepcontrol.wait,
+    // so they are complete when this kernel starts and are read before its wait
+    int pre = 0;
 };
 static_assert(alignof(GemvArgs) >= 64, "the tensor map must stay 64-byte aligned");
 
