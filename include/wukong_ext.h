@@ -114,6 +114,20 @@ int wk_model_set_tp(wk_model *m, int enable);
 int wk_predict_noalloc(int *out, const void *ff, const void *norm_weight, const void *out_weight, int batch,
                        int row, int col, int wsize, float eps, int dtype);
 
+/* Decode-step timeline (no counterpart in the reference; diagnostic build
+ * libwukong_timeline.so from `python -m wukong_b200.build --timeline`, where
+ * every GEMV and decode-attention launch records per CTA %globaltimer at its
+ * start, after griddepcontrol.wait, at phase marks and at its end; the default
+ * library returns -1 from the first two).  wk_timeline_init(slots, blocks)
+ * allocates [slots][blocks] records and restarts the count; wk_timeline_read
+ * copies info [slots][4] (kind, N, K, CTAs) and stamps [slots][blocks][9]
+ * (start, wait return, end, phases 0..5) and returns the launches recorded
+ * (launch i in slot i mod slots).  wk_timeline_resolution_ns: the smallest
+ * step of %globaltimer one thread observes. */
+int wk_timeline_init(int slots, int blocks);
+int wk_timeline_read(int *info, unsigned long long *stamps);
+long long wk_timeline_resolution_ns(void);
+
 #ifdef __cplusplus
 }
 #endif

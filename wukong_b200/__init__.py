@@ -70,6 +70,9 @@ EXT = {
     "wk_fill_const_f32": (_I, [_P, _L, _F]),
     "wk_gemv": (_I, [_P, _P, _P, _I, _I, _I, _I]),
     "wk_predict_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _F, _I]),
+    "wk_timeline_init": (_I, [_I, _I]),
+    "wk_timeline_read": (_I, [_P, _P]),
+    "wk_timeline_resolution_ns": (ctypes.c_longlong, []),
     "wk_tp_unique_id": (_I, [_P]),
     "wk_tp_init": (_I, [_I, _I, _P]),
     "wk_tp_fini": (None, []),

@@ -6,7 +6,11 @@ Outputs (in-tree, git-ignored, shipped with the source snapshot):
                              line (llm/array.go:4 links ./build/libwukong.a
                              -lcublasLt -lcudart -lm -lcublas)
 
-Usage: python -m wukong_b200.build [-j N] [--force]
+  wukong_b200/libwukong_timeline.so   with --timeline: the same library built
+                             with -DWK_TIMELINE (per-launch decode timeline,
+                             python -m wukong_b200.timeline)
+
+Usage: python -m wukong_b200.build [-j N] [--force] [--timeline]
 """
 import argparse
 import concurrent.futures as cf
@@ -20,6 +24,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 SO = os.path.join(HERE, "libwukong.so")
+TIMELINE_SO = os.path.join(HERE, "libwukong_timeline.so")
 ARCHIVE = os.path.join(ROOT, "build", "libwukong.a")
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -46,15 +51,16 @@ def _compile(src, obj, extra):
     return r.stderr
 
 
-def build(jobs=8, force=False, verbose=False, ptxas_v=False):
-    os.makedirs(OBJ, exist_ok=True)
+def build(jobs=8, force=False, verbose=False, ptxas_v=False, timeline=False):
+    obj_dir = OBJ + "_timeline" if timeline else OBJ
+    os.makedirs(obj_dir, exist_ok=True)
     os.makedirs(os.path.dirname(ARCHIVE), exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     deps = _headers()
-    extra = ["-Xptxas", "-v"] if ptxas_v else []
+    extra = (["-Xptxas", "-v"] if ptxas_v else []) + (["-DWK_TIMELINE"] if timeline else [])
     objs, todo = [], []
     for s in srcs:
-        o = os.path.join(OBJ, os.path.basename(s)[:-3] + ".o")
+        o = os.path.join(obj_dir, os.path.basename(s)[:-3] + ".o")
         objs.append(o)
         if force or ptxas_v or _stale(s, o, deps):
             todo.append((s, o))
@@ -64,6 +70,10 @@ def build(jobs=8, force=False, verbose=False, ptxas_v=False):
             msg = f.result()
             if verbose and msg:
                 print(f"== {os.path.basename(futs[f])}\n{msg}")
+    if timeline:
+        if todo or not os.path.exists(TIMELINE_SO):
+            subprocess.check_call([NVCC] + ARCH + ["-shared", "-o", TIMELINE_SO] + objs + ["-ldl"])
+        return TIMELINE_SO
     if todo or not os.path.exists(SO) or not os.path.exists(ARCHIVE):
         subprocess.check_call([NVCC] + ARCH + ["-shared", "-o", SO] + objs + ["-ldl"])
         if os.path.exists(ARCHIVE):
@@ -77,8 +87,9 @@ def main():
     p.add_argument("-j", type=int, default=8)
     p.add_argument("--force", action="store_true")
     p.add_argument("--ptxas-v", action="store_true", help="print registers / spills / shared memory per kernel")
+    p.add_argument("--timeline", action="store_true", help="build libwukong_timeline.so (-DWK_TIMELINE)")
     a = p.parse_args()
-    print(build(a.j, a.force, verbose=True, ptxas_v=a.ptxas_v))
+    print(build(a.j, a.force, verbose=True, ptxas_v=a.ptxas_v, timeline=a.timeline))
 
 
 if __name__ == "__main__":

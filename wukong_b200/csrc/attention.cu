@@ -13,6 +13,7 @@
 #include <stdlib.h>
 
 #include "common.cuh"
+#include "timeline.cuh"
 #include "wukong_internal.cuh"
 
 namespace wk {
@@ -208,6 +209,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
                                                              const int *__restrict__ pos_of_row, KVPaged kv, int G,
                                                              int Lpad_max, float scale, int *err, const void *pf,
                                                              long pf_bytes, int early) {
+    Timeline tl;
     constexpr int kPageBytes = kAttnPage * D * 2;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *ring = smem;                                                      // [slots][64][D] T
@@ -263,6 +265,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     }
     pdl_wait();
     pdl_trigger();
+    tl.mark(100, npages, G);
     if (!early) {
         for (int i = tid; i < npages; i += 128) pgs[i] = bt[i];
         __syncthreads();
@@ -277,6 +280,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     const T *qrow = q + (long)row * q_rs + (long)kvh * G * D;
     for (int i = tid; i < 8 * D; i += 128) qs[i] = i < G * D ? qrow[i] : from_float<T>(0.f);
     __syncthreads();
+    tl.phase(0);  // q staged
     uint32_t qb[D / 16][2];
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
@@ -321,6 +325,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
             ++issued;
         }
     }
+    tl.phase(1);  // scores
     // max over the 8 lanes sharing t (g = 0..7), then over warps
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
@@ -373,6 +378,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
         }
     __syncthreads();
 
+    tl.phase(2);  // softmax
     // ---- pass 2: O^T = V^T . P^T; warp w owns d-tiles w, w + 4
     constexpr int kDT = D / 16;
     float o[kDT > 4 ? 2 : 1][4];
@@ -417,6 +423,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
             ++issued;
         }
     }
+    tl.phase(3);  // P.V
     // o[a]: rows d0 + g, d0 + g + 8; columns (heads) 2t, 2t + 1
     T *orow = out + (long)row * out_rs + (long)kvh * G * D;
 #pragma unroll
@@ -449,6 +456,7 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
                                                                 int pps, int lpad, float scale, T *__restrict__ S,
                                                                 float *__restrict__ mpart, float *__restrict__ minv,
                                                                 int *__restrict__ counter, int *err, int early) {
+    Timeline tl;
     constexpr int kPageBytes = kAttnPage * D * 2;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *ring = smem;
@@ -483,6 +491,7 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
         }
     pdl_wait();
     pdl_trigger();
+    tl.mark(101, npages, nz);
     if (tid == 0)
         for (; issued < kAttnSlots && issued < n; ++issued) {
             mbar_expect_tx(bars + issued, kPageBytes);
@@ -551,6 +560,7 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
     __shared__ int last;
     __threadfence();
     __syncthreads();
+    tl.phase(0);  // scores of this split
     if (tid == 0) last = atomicAdd(counter + rh, 1) == nz - 1;
     __syncthreads();
     if (!last) return;
@@ -558,25 +568,51 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
     const int Lpad = npages * kAttnPage;
     T *ss = reinterpret_cast<T *>(qs + 8 * D);  // [8][Lpad] staged scores
     {
+        // eight 16-byte loads in flight per thread
         const uint4 *src = reinterpret_cast<const uint4 *>(S + rh * 8 * lpad);
         const int per_head = Lpad * (int)sizeof(T) / 16, stride = lpad * (int)sizeof(T) / 16;
-        for (int i = tid; i < 8 * per_head; i += 128) {
-            const int h = i / per_head, c = i - h * per_head;
-            reinterpret_cast<uint4 *>(ss)[h * per_head + c] = __ldcg(src + h * stride + c);
+        const int total = 8 * per_head;
+        for (int i0 = tid; i0 < total; i0 += 8 * 128) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = i0 + u * 128, h = i / per_head;
+                if (i < total) v[u] = __ldcg(src + h * stride + (i - h * per_head));
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (i0 + u * 128 < total) reinterpret_cast<uint4 *>(ss)[i0 + u * 128] = v[u];
         }
     }
     float *Ms = red;  // [8]
     if (tid < 8) {
         float m = -INFINITY;
-        for (int zz = 0; zz < nz; ++zz) m = fmaxf(m, __ldcg(mpart + (rh * nz + zz) * 8 + tid));
+        for (int z0 = 0; z0 < nz; z0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = z0 + u < nz ? __ldcg(mpart + (rh * nz + z0 + u) * 8 + tid) : -INFINITY;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) m = fmaxf(m, v[u]);
+        }
         Ms[tid] = m;
     }
     __syncthreads();
+    tl.phase(1);  // row staged
     const int h = tid >> 4, i0 = tid & 15;
     const float M = Ms[h];
     float lsum = 0.f;
-    for (int j = i0; j < Lpad; j += 16)
-        if (j < L && h < G) lsum += expf(to_float(ss[h * Lpad + j]) * scale - M);
+    // keys j = i0 + 16 u, eight at a time, summed in ascending j
+    for (int j0 = i0; j0 < Lpad; j0 += 16 * 8) {
+        float e[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = j0 + 16 * u;
+            e[u] = j < L && h < G ? to_float(ss[h * Lpad + j]) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (j0 + 16 * u < L && h < G) lsum += expf(e[u] * scale - M);
+    }
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
     if (i0 == 0) {
@@ -584,6 +620,7 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
         minv[rh * 16 + 2 * h + 1] = 1.0f / lsum;
     }
     if (tid == 0) counter[rh] = 0;
+    tl.phase(2);  // normaliser
 }
 
 template <typename T, int D>
@@ -593,6 +630,7 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
                                                             int pps, int lpad, float scale, const T *__restrict__ S,
                                                             const float *__restrict__ minv, float *__restrict__ opart,
                                                             int *__restrict__ counter, int *err, int early) {
+    Timeline tl;
     constexpr int kPageBytes = kAttnPage * D * 2;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *ring = smem;
@@ -629,6 +667,7 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
         }
     pdl_wait();
     pdl_trigger();
+    tl.mark(102, npages, nz);
     if (tid == 0)
         for (; issued < kAttnSlots && issued < n; ++issued) {
             mbar_expect_tx(bars + issued, kPageBytes);
@@ -640,15 +679,26 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
         const int h = tid >> 4, i0 = tid & 15;
         const T *sr = S + (rh * 8 + h) * lpad;
         const float M = minv[rh * 16 + 2 * h], inv = minv[rh * 16 + 2 * h + 1];
-        for (int jj = i0; jj < n * kAttnPage; jj += 16) {
-            const int j = p0 * kAttnPage + jj;
-            float pv = 0.f;
-            if (j < L && h < G)
-                pv = to_float(from_float<T>(to_float(from_float<T>(expf(to_float(sr[j]) * scale - M))) * inv));
-            pl[h * wl + jj] = from_float<T>(pv);
+        for (int jj0 = i0; jj0 < n * kAttnPage; jj0 += 16 * 8) {  // eight loads in flight
+            float sv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int j = p0 * kAttnPage + jj0 + 16 * u;
+                sv[u] = jj0 + 16 * u < n * kAttnPage && j < L && h < G ? to_float(sr[j]) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int jj = jj0 + 16 * u, j = p0 * kAttnPage + jj;
+                if (jj >= n * kAttnPage) continue;
+                float pv = 0.f;
+                if (j < L && h < G)
+                    pv = to_float(from_float<T>(to_float(from_float<T>(expf(sv[u] * scale - M))) * inv));
+                pl[h * wl + jj] = from_float<T>(pv);
+            }
         }
     }
     __syncthreads();
+    tl.phase(0);  // P of this split
     constexpr int kDT = D / 16;
     constexpr int kNA = kDT > 4 ? 2 : 1;
     float o[kNA][4];
@@ -705,17 +755,27 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
     }
     __threadfence();
     __syncthreads();
+    tl.phase(1);  // partial of this split
     if (tid == 0) last = atomicAdd(counter + rh, 1) == nz - 1;
     __syncthreads();
     if (!last) return;
     __threadfence();
     T *orow = out + (long)row * out_rs + (long)kvh * G * D;
     for (int i = tid; i < G * D; i += 128) {
+        // partials added in split order, eight loads in flight
         float acc = 0.f;
-        for (int zz = 0; zz < nz; ++zz) acc += __ldcg(opart + (rh * nz + zz) * 8 * D + i);
+        for (int z0 = 0; z0 < nz; z0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = z0 + u < nz ? __ldcg(opart + (rh * nz + z0 + u) * 8 * D + i) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (z0 + u < nz) acc += v[u];
+        }
         orow[i] = from_float<T>(acc);
     }
     if (tid == 0) counter[rh] = 0;
+    tl.phase(2);  // combined
 }
 
 template <typename T, int D>
@@ -851,6 +911,12 @@ template void attention_qkv_rows<float>(float *, const float *, int, int, int, i
 template void attention_qkv_rows<__half>(__half *, const __half *, int, int, int, int, int, cudaStream_t);
 template void attention_qkv_rows<__nv_bfloat16>(__nv_bfloat16 *, const __nv_bfloat16 *, int, int, int, int, int,
                                                 cudaStream_t);
+
+#ifdef WK_TIMELINE
+void timeline_bind_attn(const TimelineBuf &b) { WK_CHECK(cudaMemcpyToSymbol(c_tl, &b, sizeof b)); }
+#else
+void timeline_bind_attn(const TimelineBuf &) {}
+#endif
 
 }  // namespace wk
 

@@ -26,6 +26,7 @@
 //    paged cache, applies SwiGLU, or reduces logits to an argmax.
 //  * An optional RMSNorm prologue normalises X while staging it in shared memory.
 #include "common.cuh"
+#include "timeline.cuh"
 #include "wukong_internal.cuh"
 
 namespace wk {
@@ -269,6 +270,7 @@ __device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad, const Norm
     for (int m = wid; m < M; m += kWarps) {
         const T *xr = xs + (long)m * Kpad;
         float ss = 0.f;
+#pragma unroll 8
         for (int k = lane; k < a.K; k += 32) {
             float v = to_float(xr[k]);
             ss += v * v;
@@ -436,6 +438,7 @@ __device__ __forceinline__ void warp_epilogue(const GemvArgs &a, int tile, int g
 
 template <typename T, int WT, int NS>
 __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
+    Timeline tl;
     using F = WFmt<WT>;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int nchunks = (a.K + F::kChunk - 1) / F::kChunk;
@@ -490,8 +493,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     // in the stream start its own weight prefetch
     pdl_wait();
     pdl_trigger();
+    tl.mark(a.epi, a.N, a.K);
     if (stage) stage_xn<T>(a, sm, Kpad, normw);
     __syncthreads();
+    tl.phase(0);  // activations staged (and normalised)
 
     float best_v = -INFINITY;
     uint64_t best_k = ~0ull;
@@ -559,8 +564,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
                     issue_unit<WT>(a, sm, w, slot, tile, chunk, lane, false, NS);
                     __syncwarp();
                 }
+                if (w == 0) tl.phase(1);  // first unit landed
                 if (ok) consume_unit<WT>(a, sm, w, slot, chunk, lane, c, NS);
                 __syncwarp();  // the slot is free again
+                if (w == 0) tl.phase(2);  // first unit consumed
                 ++consumed;
                 if (tma && ok)
                     produce_unit<WT>(a, sm, w, slot, lane, has_work, ntiles, nchunks, p_tile, p_chunk, cstart, cstep,
@@ -577,8 +584,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         __syncthreads();
         epilogue<T>(a, sm.red, tile, best_v, best_k, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
         __syncthreads();  // red is rewritten by the next tile
+        tl.phase(3);          // first tile stored
     }
 
+    tl.phase(4);  // all tiles
     if (a.epi == EPI_LOGITS) {
         // per-CTA argmax partials: reduce over the 16 row-threads of each column m
         const int tid = threadIdx.x, m = tid & 7;
@@ -746,5 +755,11 @@ void gemv(GemvArgs a, int act, cudaStream_t s) {
             launch<__nv_bfloat16, kBF16, kStages>(a, grid, smem_used, s, pdl);
     }
 }
+
+#ifdef WK_TIMELINE
+void timeline_bind_gemv(const TimelineBuf &b) { WK_CHECK(cudaMemcpyToSymbol(c_tl, &b, sizeof b)); }
+#else
+void timeline_bind_gemv(const TimelineBuf &) {}
+#endif
 
 }  // namespace wk
