@@ -441,13 +441,15 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
 // ---------------------------------------------------------------- split-K decode attention
 // For few (row, kv head) pairs and long contexts the pages are split over
 // gridDim.z CTAs in two launches with the reference's rounding points intact:
-//   scores:  s_j = T(q . k_j) of this split's keys -> global score rows, and the
-//            split's max of s_j * scale per head;
-//   pv:      every split CTA takes M = max over splits and the softmax sum over
-//            the whole row in the single-CTA kernel's order (same e_j, same sum,
-//            same P_j = T(T(e_j) / sum)), multiplies its own V pages, writes an
-//            fp32 partial, and the last CTA of the (row, head) adds the partials
-//            in split order and stores T(o).
+//   scores:  s_j = T(q . k_j) of this split's keys -> global score rows, the
+//            split's max m_z of s_j * scale per head and l_z = sum of
+//            exp(s_j * scale - m_z) over its keys; the last CTA of the (row,
+//            head) forms M = max m_z and sum = sum_z l_z exp(m_z - M) in split
+//            order (the same softmax sum, factored by split);
+//   pv:      every split CTA takes P_j = T(T(exp(s_j * scale - M)) / sum) for
+//            its keys, multiplies its own V pages, writes an fp32 partial, and
+//            the last CTA of the (row, head) adds the partials in split order
+//            and stores T(o).
 
 template <typename T, int D>
 __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restrict__ q, long q_rs,
@@ -507,6 +509,8 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
         qb[kk][1] = *reinterpret_cast<const uint32_t *>(qs + g * D + kk * 16 + 2 * t + 8);
     }
     T *srow = S + ((long)row * kv.kv_heads + kvh) * 8 * lpad;
+    T *own = qs + 8 * D;  // [8][pps * 64] this split's scores
+    const int wl = pps * kAttnPage;
     float mx0 = -INFINITY, mx1 = -INFINITY;
     bool ok = true;
     for (int i = 0; i < n; ++i) {
@@ -528,6 +532,7 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
             const int key = k0 + (j >> 1) * 8, h = 2 * t + (j & 1);
             const float sv = key < L ? round_to<T>(c[j]) : -INFINITY;
             srow[(long)h * lpad + key] = from_float<T>(key < L ? sv : 0.f);
+            own[h * wl + key - p0 * kAttnPage] = from_float<T>(key < L ? sv : 0.f);
             if (j & 1)
                 mx1 = fmaxf(mx1, sv * scale);
             else
@@ -552,11 +557,36 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
     }
     __syncthreads();
     const long rh = (long)row * kv.kv_heads + kvh;
-    if (tid < 8)
-        mpart[(rh * nz + z) * 8 + tid] =
-            fmaxf(fmaxf(red[tid * 4], red[tid * 4 + 1]), fmaxf(red[tid * 4 + 2], red[tid * 4 + 3]));
-    // the last split of this (row, head) computes the softmax normaliser of the
-    // whole row, in the single-CTA kernel's order, for the P.V launch
+    // this split's max and sum of exp(s * scale - max) per head over its own keys
+    __shared__ float s_m[8];
+    if (tid < 8) s_m[tid] = fmaxf(fmaxf(red[tid * 4], red[tid * 4 + 1]), fmaxf(red[tid * 4 + 2], red[tid * 4 + 3]));
+    __syncthreads();
+    {
+        const int h = tid >> 4, i0 = tid & 15;  // 16 threads per head, keys i0, i0 + 16, ...
+        const float mz = s_m[h];
+        float lsum = 0.f;
+        for (int j0 = i0; j0 < n * kAttnPage; j0 += 16 * 8) {
+            float e[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int jj = j0 + 16 * u;
+                e[u] = jj < n * kAttnPage && p0 * kAttnPage + jj < L && h < G ? to_float(own[h * wl + jj]) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int jj = j0 + 16 * u;
+                if (jj < n * kAttnPage && p0 * kAttnPage + jj < L && h < G) lsum += expf(e[u] * scale - mz);
+            }
+        }
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+        if (i0 == 0) {
+            mpart[(rh * nz + z) * 16 + h] = mz;
+            mpart[(rh * nz + z) * 16 + 8 + h] = lsum;
+        }
+    }
+    // the last split of this (row, head) combines the splits' (max, sum) pairs
+    // in split order: M = max_z m_z, sum = sum_z l_z exp(m_z - M)
     __shared__ int last;
     __threadfence();
     __syncthreads();
@@ -565,59 +595,31 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
     __syncthreads();
     if (!last) return;
     __threadfence();
-    const int Lpad = npages * kAttnPage;
-    T *ss = reinterpret_cast<T *>(qs + 8 * D);  // [8][Lpad] staged scores
+    // all splits' (max, sum) pairs into the page ring (free now) in one round trip
+    float *pairs = reinterpret_cast<float *>(ring);  // [nz][16]
     {
-        // eight 16-byte loads in flight per thread
-        const uint4 *src = reinterpret_cast<const uint4 *>(S + rh * 8 * lpad);
-        const int per_head = Lpad * (int)sizeof(T) / 16, stride = lpad * (int)sizeof(T) / 16;
-        const int total = 8 * per_head;
-        for (int i0 = tid; i0 < total; i0 += 8 * 128) {
-            uint4 v[8];
+        const float4 *src = reinterpret_cast<const float4 *>(mpart + rh * nz * 16);
+        for (int i0 = tid; i0 < nz * 4; i0 += 4 * 128) {
+            float4 v[4];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int i = i0 + u * 128, h = i / per_head;
-                if (i < total) v[u] = __ldcg(src + h * stride + (i - h * per_head));
-            }
+            for (int u = 0; u < 4; ++u)
+                if (i0 + u * 128 < nz * 4) v[u] = __ldcg(src + i0 + u * 128);
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (i0 + u * 128 < total) reinterpret_cast<uint4 *>(ss)[i0 + u * 128] = v[u];
+            for (int u = 0; u < 4; ++u)
+                if (i0 + u * 128 < nz * 4) reinterpret_cast<float4 *>(pairs)[i0 + u * 128] = v[u];
         }
-    }
-    float *Ms = red;  // [8]
-    if (tid < 8) {
-        float m = -INFINITY;
-        for (int z0 = 0; z0 < nz; z0 += 8) {
-            float v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = z0 + u < nz ? __ldcg(mpart + (rh * nz + z0 + u) * 8 + tid) : -INFINITY;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) m = fmaxf(m, v[u]);
-        }
-        Ms[tid] = m;
     }
     __syncthreads();
-    tl.phase(1);  // row staged
-    const int h = tid >> 4, i0 = tid & 15;
-    const float M = Ms[h];
-    float lsum = 0.f;
-    // keys j = i0 + 16 u, eight at a time, summed in ascending j
-    for (int j0 = i0; j0 < Lpad; j0 += 16 * 8) {
-        float e[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int j = j0 + 16 * u;
-            e[u] = j < L && h < G ? to_float(ss[h * Lpad + j]) : 0.f;
+    if (tid < 8) {
+        float M = -INFINITY;
+        for (int zz = 0; zz < nz; ++zz) M = fmaxf(M, pairs[zz * 16 + tid]);
+        float sum = 0.f;
+        for (int zz = 0; zz < nz; ++zz) {
+            const float l = pairs[zz * 16 + 8 + tid];
+            if (l > 0.f) sum += l * expf(pairs[zz * 16 + tid] - M);
         }
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if (j0 + 16 * u < L && h < G) lsum += expf(e[u] * scale - M);
-    }
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-    if (i0 == 0) {
-        minv[rh * 16 + 2 * h] = M;
-        minv[rh * 16 + 2 * h + 1] = 1.0f / lsum;
+        minv[rh * 16 + 2 * tid] = M;
+        minv[rh * 16 + 2 * tid + 1] = 1.0f / sum;
     }
     if (tid == 0) counter[rh] = 0;
     tl.phase(2);  // normaliser
@@ -761,18 +763,28 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
     if (!last) return;
     __threadfence();
     T *orow = out + (long)row * out_rs + (long)kvh * G * D;
-    for (int i = tid; i < G * D; i += 128) {
-        // partials added in split order, eight loads in flight
-        float acc = 0.f;
-        for (int z0 = 0; z0 < nz; z0 += 8) {
-            float v[8];
+    for (int i4 = tid; i4 < G * D / 4; i4 += 128) {
+        // four outputs per thread, partials added in split order, sixteen loads in flight
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int z0 = 0; z0 < nz; z0 += 16) {
+            float4 v[16];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = z0 + u < nz ? __ldcg(opart + (rh * nz + z0 + u) * 8 * D + i) : 0.f;
+            for (int u = 0; u < 16; ++u)
+                v[u] = z0 + u < nz ? __ldcg(reinterpret_cast<const float4 *>(opart + (rh * nz + z0 + u) * 8 * D) + i4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (z0 + u < nz) acc += v[u];
+            for (int u = 0; u < 16; ++u)
+                if (z0 + u < nz) {
+                    acc.x += v[u].x;
+                    acc.y += v[u].y;
+                    acc.z += v[u].z;
+                    acc.w += v[u].w;
+                }
         }
-        orow[i] = from_float<T>(acc);
+        orow[4 * i4] = from_float<T>(acc.x);
+        orow[4 * i4 + 1] = from_float<T>(acc.y);
+        orow[4 * i4 + 2] = from_float<T>(acc.z);
+        orow[4 * i4 + 3] = from_float<T>(acc.w);
     }
     if (tid == 0) counter[rh] = 0;
     tl.phase(2);  // combined
@@ -797,7 +809,7 @@ bool launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_
     if (nz < 2) return false;
     const float scale = 1.0f / sqrtf((float)D);
     const size_t smem_a = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 32 * 4 + 8 * D * 2 +
-                          (size_t)8 * pages * kAttnPage * 2;
+                          (size_t)8 * pps * kAttnPage * 2;
     const size_t smem_b = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + (size_t)8 * pps * kAttnPage * 2;
     if ((int)smem_a > g_rt.max_smem_optin || (int)smem_b > g_rt.max_smem_optin) return false;
     auto ka = attn_split_scores_kernel<T, D>;

@@ -637,7 +637,7 @@ int wk_model_alloc_cache(wk_model *m, int max_batch, int max_ctx) {
         w.lpad = m->max_pages * kPage;
         const size_t rh = (size_t)max_batch * c.n_kv_heads;
         WK_TRY(cudaMallocAsync(&w.scores, rh * 8 * w.lpad * act_size(m->act), s));
-        WK_TRY(cudaMallocAsync((void **)&w.mpart, rh * w.max_splits * 8 * sizeof(float), s));
+        WK_TRY(cudaMallocAsync((void **)&w.mpart, rh * w.max_splits * 16 * sizeof(float), s));
         WK_TRY(cudaMallocAsync((void **)&w.opart, rh * w.max_splits * 8 * c.head_dim * sizeof(float), s));
         WK_TRY(cudaMallocAsync((void **)&w.counter, 2 * rh * sizeof(int), s));
         WK_TRY(cudaMemsetAsync(w.counter, 0, 2 * rh * sizeof(int), s));

@@ -138,7 +138,7 @@ struct PagedKV {
 // Scratch of split-K decode attention (sized by its owner; counter zeroed once).
 struct AttnSplitWs {
     void *scores = nullptr;     // [max_rows][max_kv_heads][8][lpad] (type T)
-    float *mpart = nullptr;     // [max_rows][max_kv_heads][max_splits][8]
+    float *mpart = nullptr;     // [max_rows][max_kv_heads][max_splits][16]: 8 maxima, 8 sums of exp(s - max)
     float *opart = nullptr;     // [max_rows][max_kv_heads][max_splits][8][head_dim]
     int *counter = nullptr;     // [max_rows][max_kv_heads], zero between launches (P.V launch)
     int *counter_a = nullptr;   // the same for the scores launch
