@@ -179,13 +179,14 @@ void launch_rows(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_r
 //   S^T[16 keys x 8 heads] = K[16 keys x D] . Q^T[D x 8 heads]   (A by ldmatrix)
 //   O^T[16 d x 8 heads]    = V^T[16 d x keys] . P^T[keys x 8]     (A by ldmatrix.trans)
 // K and V pages ([page][kv_head][64 tokens][D], 8 or 16 KB contiguous per head)
-// stream through a 4-slot shared-memory ring by 1-D bulk copies; pages that
+// stream through a shared-memory ring of up to 64 KB by 1-D bulk copies; pages that
 // precede the newest token's page were written by earlier launches and are
 // requested before griddepcontrol.wait.  Between the two GEMM passes the
 // softmax runs on the fp16 score row kept in shared memory with the
 // reference's rounding points (see the file header).
 constexpr int kAttnPage = 64;
-constexpr int kAttnSlots = 4;
+constexpr int kAttnSlots = 4;     // ring slots of the split-K kernels
+constexpr int kAttnMaxSlots = 8;  // of the decode kernel: up to 64 KB of pages, fewer for long contexts
 
 template <typename T> struct IsBF16 {
     static constexpr bool value = false;
@@ -203,7 +204,7 @@ __device__ __forceinline__ void mma16(float (&c)[4], uint32_t a0, uint32_t a1, u
         mma_f16(c, a0, a1, a2, a3, b0, b1);
 }
 
-template <typename T, int D>
+template <typename T, int D, int S>
 __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out, long out_rs, const T *__restrict__ q,
                                                              long q_rs, const int *__restrict__ seq_of_row,
                                                              const int *__restrict__ pos_of_row, KVPaged kv, int G,
@@ -213,8 +214,8 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     constexpr int kPageBytes = kAttnPage * D * 2;
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *ring = smem;                                                      // [slots][64][D] T
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnSlots * kPageBytes);
-    float *red = reinterpret_cast<float *>(bars + kAttnSlots);                // [8 heads][4 warps]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + S * kPageBytes);   // S <= kAttnMaxSlots
+    float *red = reinterpret_cast<float *>(bars + kAttnMaxSlots);             // [8 heads][4 warps]
     T *qs = reinterpret_cast<T *>(red + 64);                                  // [8][D]
     T *sc = qs + 8 * D;                                                       // [8][Lpad_max] scores -> P
 
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     };
     if (tid == 64 && pf)
         l2_prefetch_slice(pf, pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
-    if (tid < kAttnSlots) mbar_init(bars + tid, 1);
+    if (tid < S) mbar_init(bars + tid, 1);
     // decode: the block table is not written by the producing kernel
     if (early)
         for (int i = tid; i < npages; i += 128) pgs[i] = bt[i];
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     // this call) that kernel may still be writing them.
     int issued = 0;
     if (tid == 0 && early) {
-        for (; issued < kAttnSlots && issued < npages - 1; ++issued) {
+        for (; issued < S && issued < npages - 1; ++issued) {
             mbar_expect_tx(bars + issued, kPageBytes);
             bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
         }
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
         __syncthreads();
     }
     if (tid == 0) {
-        for (; issued < kAttnSlots && issued < total; ++issued) {
+        for (; issued < S && issued < total; ++issued) {
             mbar_expect_tx(bars + issued, kPageBytes);
             bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
         }
@@ -293,8 +294,8 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     int consumed = 0;
     bool ok = true;
     for (int p = 0; p < npages; ++p, ++consumed) {
-        const int slot = consumed % kAttnSlots;
-        if (!mbar_wait_bounded(bars + slot, (consumed / kAttnSlots) & 1, err, 3)) ok = false;
+        const int slot = consumed % S;
+        if (!mbar_wait_bounded(bars + slot, (consumed / S) & 1, err, 3)) ok = false;
         const T *kt = reinterpret_cast<const T *>(ring + slot * kPageBytes) + warp * 16 * D;
         float c[4] = {0.f, 0.f, 0.f, 0.f};
         if (ok) {
@@ -319,7 +320,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
         }
         __syncthreads();  // everyone is done with this slot
         if (tid == 0 && issued < total) {
-            const int sl = issued % kAttnSlots;
+            const int sl = issued % S;
             mbar_expect_tx(bars + sl, kPageBytes);
             bulk_g2s(ring + sl * kPageBytes, page_src(issued), kPageBytes, bars + sl);
             ++issued;
@@ -385,8 +386,8 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
 #pragma unroll
     for (int a = 0; a < (kDT > 4 ? 2 : 1); ++a) o[a][0] = o[a][1] = o[a][2] = o[a][3] = 0.f;
     for (int p = 0; p < npages; ++p, ++consumed) {
-        const int slot = consumed % kAttnSlots;
-        if (!mbar_wait_bounded(bars + slot, (consumed / kAttnSlots) & 1, err, 3)) ok = false;
+        const int slot = consumed % S;
+        if (!mbar_wait_bounded(bars + slot, (consumed / S) & 1, err, 3)) ok = false;
         if (p == npages - 1 && L % kAttnPage) {
             // rows past the sequence end hold stale cache bytes; their P is 0, but 0 * NaN is NaN
             T *vw = reinterpret_cast<T *>(ring + slot * kPageBytes);
@@ -417,7 +418,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
         }
         __syncthreads();
         if (tid == 0 && issued < total) {
-            const int sl = issued % kAttnSlots;
+            const int sl = issued % S;
             mbar_expect_tx(bars + sl, kPageBytes);
             bulk_g2s(ring + sl * kPageBytes, page_src(issued), kPageBytes, bars + sl);
             ++issued;
@@ -848,14 +849,18 @@ void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq
                       int nrows, int max_len, const KVPaged &kv, int G, cudaStream_t s, bool pdl, const void *pf,
                       long pf_bytes, bool early) {
     const int Lpad = (max_len + kAttnPage - 1) / kAttnPage * kAttnPage;
-    const size_t smem = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 64 * 4 + 8 * D * 2 +
-                        (size_t)8 * Lpad * 2 + (size_t)(Lpad / kAttnPage) * 4;
+    constexpr size_t kPageBytes = (size_t)kAttnPage * D * 2;
+    const size_t fixed = kAttnMaxSlots * 8 + 64 * 4 + 8 * D * 2 + (size_t)8 * Lpad * 2 + (size_t)(Lpad / kAttnPage) * 4;
+    int S = (int)(64 * 1024 / kPageBytes);
+    if (S > kAttnMaxSlots) S = kAttnMaxSlots;
+    if (S < kAttnMaxSlots || fixed + S * kPageBytes > (size_t)g_rt.max_smem_optin) S = kAttnSlots;
+    const size_t smem = fixed + S * kPageBytes;
     if ((int)smem > g_rt.max_smem_optin) WK_PANIC("attention: context %d needs %zu B of shared memory", max_len, smem);
-    auto kern = attn_decode_tc_kernel<T, D>;
-    static int configured = 0;
-    if ((int)smem > configured) {
+    auto kern = S == kAttnMaxSlots ? attn_decode_tc_kernel<T, D, kAttnMaxSlots> : attn_decode_tc_kernel<T, D, kAttnSlots>;
+    static int configured[2] = {0, 0};
+    if ((int)smem > configured[S == kAttnMaxSlots]) {
         WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        configured = (int)smem;
+        configured[S == kAttnMaxSlots] = (int)smem;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kv.kv_heads, nrows);
