@@ -225,35 +225,66 @@ __device__ __forceinline__ void norm_pre(const GemvArgs &a, NormW &nw) {
 
 // RMSNorm prologue: normalise X, rounded to T as the reference stores its
 // rmsnorm output (cuda.cu:533-601), into shared memory [M][Kpad] (zero padded).
-// The rows are copied in with 8-byte loads first (one round trip instead of a
-// dependent load per element), then summed from shared memory in the same
-// order (lane l adds elements l, l + 32, ...) and normalised in place.
+// Sum-of-squares order (the persistent kernel follows it too): thread t adds
+// the quads (4 consecutive values) k/4 = t, t + 256, ... of a row in that order,
+// its warp sums the threads by butterfly, then the 8 warps' sums are added in
+// warp order.  One row (decode) with K <= 4096 stays in registers from the load
+// to the normalised store; more rows go through shared memory in the same order.
 template <typename T>
-__device__ __forceinline__ void norm_quad(const GemvArgs &a, const Smem &sm, int nq, int kq, float4 w) {
-    for (int m = 0; m < a.M; ++m) {
-        const int i = m * nq + kq;
-        const uint2 r = sm.xn[i];
-        const T *rv = reinterpret_cast<const T *>(&r);
-        const float wv[4] = {w.x, w.y, w.z, w.w};
-        float v[4];
+__device__ __forceinline__ void quad_ss(uint2 q, float &ss) {
+    const T *e = reinterpret_cast<const T *>(&q);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = (to_float(rv[j]) * sm.misc[m]) * wv[j];
-        uint2 pk;
-        pk.x = pack2<T>(v[0], v[1]);
-        pk.y = pack2<T>(v[2], v[3]);
-        sm.xn[i] = pk;
+    for (int j = 0; j < 4; ++j) {
+        const float f = to_float(e[j]);
+        ss += f * f;
     }
+}
+template <typename T>
+__device__ __forceinline__ uint2 quad_norm(uint2 q, float r, float4 w) {
+    const T *e = reinterpret_cast<const T *>(&q);
+    uint2 pk;
+    pk.x = pack2<T>((to_float(e[0]) * r) * w.x, (to_float(e[1]) * r) * w.y);
+    pk.y = pack2<T>((to_float(e[2]) * r) * w.z, (to_float(e[3]) * r) * w.w);
+    return pk;
 }
 template <typename T>
 __device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad, const NormW &nw) {
     const int M = a.M;
     const T *x = reinterpret_cast<const T *>(a.x);
-    const int nq = Kpad / 4, total = nq * M, nt = blockDim.x;
+    const int nq = Kpad / 4, total = nq * M, nt = blockDim.x, tid = threadIdx.x;
+    const int wid = tid >> 5, lane = tid & 31;
+    const int kq_end = a.K / 4;  // quads holding data (K is a multiple of 16)
     auto ld = [&](int i) -> uint2 {
         const int m = i / nq, k = (i - m * nq) * 4;
         return k < a.K ? *reinterpret_cast<const uint2 *>(x + (long)m * a.ldx + k) : make_uint2(0u, 0u);
     };
-    for (int i = threadIdx.x; i < total; i += 8 * nt) {  // up to 8 loads in flight per thread
+    float *wsum = sm.red;  // [8 warps][8 rows] (the tiles use sm.red only later)
+    if (a.norm_w && M == 1 && nq <= kNormRegs * nt) {
+        uint2 v[kNormRegs];
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < kNormRegs; ++j) {
+            const int kq = tid + j * nt;
+            v[j] = kq < nq ? ld(kq) : make_uint2(0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < kNormRegs; ++j)
+            if (tid + j * nt < kq_end) quad_ss<T>(v[j], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) wsum[wid * 8] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) tot += wsum[w * 8];
+        const float r = rsqrtf(tot / (float)a.K + a.eps);
+#pragma unroll
+        for (int j = 0; j < kNormRegs; ++j) {
+            const int kq = tid + j * nt;
+            if (kq < nq) sm.xn[kq] = kq < kq_end ? quad_norm<T>(v[j], r, nw.v[j]) : make_uint2(0u, 0u);
+        }
+        return;  // the caller's barrier publishes the rows
+    }
+    for (int i = tid; i < total; i += 8 * nt) {  // up to 8 loads in flight per thread
         uint2 v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -264,29 +295,26 @@ __device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad, const Norm
     }
     __syncthreads();
     if (!a.norm_w) return;
-    const T *xs = reinterpret_cast<const T *>(sm.xn);
-    // one warp per activation row: sum of squares
-    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int m = wid; m < M; m += kWarps) {
-        const T *xr = xs + (long)m * Kpad;
+    for (int m = 0; m < M; ++m) {
         float ss = 0.f;
-#pragma unroll 8
-        for (int k = lane; k < a.K; k += 32) {
-            float v = to_float(xr[k]);
-            ss += v * v;
-        }
+        for (int kq = tid; kq < kq_end; kq += nt) quad_ss<T>(sm.xn[m * nq + kq], ss);
         ss = warp_sum(ss);
-        if (lane == 0) sm.misc[m] = rsqrtf(ss / (float)a.K + a.eps);
+        if (lane == 0) wsum[wid * 8 + m] = ss;
     }
     __syncthreads();
-    // normalise in place; the zero padding (k >= K) stays zero
+    for (int m = 0; m < M; ++m) {
+        float tot = 0.f;
 #pragma unroll
-    for (int j = 0; j < kNormRegs; ++j) {
-        const int kq = threadIdx.x + j * blockDim.x;
-        if (kq * 4 < a.K) norm_quad<T>(a, sm, nq, kq, nw.v[j]);
+        for (int w = 0; w < kWarps; ++w) tot += wsum[w * 8 + m];
+        const float r = rsqrtf(tot / (float)a.K + a.eps);
+#pragma unroll
+        for (int j = 0; j < kNormRegs; ++j) {
+            const int kq = tid + j * nt;
+            if (kq < kq_end) sm.xn[m * nq + kq] = quad_norm<T>(sm.xn[m * nq + kq], r, nw.v[j]);
+        }
+        for (int kq = tid + kNormRegs * nt; kq < kq_end; kq += nt)
+            sm.xn[m * nq + kq] = quad_norm<T>(sm.xn[m * nq + kq], r, load_norm4(a.norm_w, kq * 4));
     }
-    for (int kq = threadIdx.x + kNormRegs * blockDim.x; kq * 4 < a.K; kq += blockDim.x)
-        norm_quad<T>(a, sm, nq, kq, load_norm4(a.norm_w, kq * 4));
 }
 
 // Threads 0..127 own one (row r, column m) output of the 16 x 8 tile; `red`

@@ -239,8 +239,8 @@ __device__ void mk_embed(const MkArgs &a) {
 
 // RMSNorm of x rows into shared memory, rounded to half (cuda.cu:533-601).
 // x is copied in with 16-byte loads first (one L2 round trip), then the sums
-// of squares run over shared memory in the GEMV prologue's order (lane l adds
-// elements l, l + 32, ...), so the result is bit-identical to it.
+// of squares run over shared memory in the GEMV prologue's order, so the
+// result is bit-identical to it.
 __device__ void mk_stage_norm(const MkArgs &a, const Sm &sm, const float *nw) {
     const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint4 *raw = reinterpret_cast<uint4 *>(sm.work);
@@ -248,21 +248,34 @@ __device__ void mk_stage_norm(const MkArgs &a, const Sm &sm, const float *nw) {
     const int n16 = a.B * a.d / 8;
     for (int i = threadIdx.x; i < n16; i += kThreads) raw[i] = __ldcg(xg + i);
     __syncthreads();
-    const __half *xh = reinterpret_cast<const __half *>(sm.work);
-    for (int m = wid; m < a.B; m += kW) {
-        const __half *xr = xh + (long)m * a.d;
+    // sums of squares in the GEMV prologue's order: thread t adds the quads
+    // t, t + 256, ... of a row, its warp sums by butterfly, then the 8 warps'
+    // sums are added in warp order
+    __shared__ float wsum[kW * 8];
+    const int nq = a.d / 4;
+    uint2 *xs = reinterpret_cast<uint2 *>(sm.work);
+    for (int m = 0; m < a.B; ++m) {
         float ss = 0.f;
-        for (int k = lane; k < a.d; k += 32) {
-            const float v = __half2float(xr[k]);
-            ss += v * v;
+        for (int kq = threadIdx.x; kq < nq; kq += kThreads) {
+            const uint2 r = xs[m * nq + kq];
+            const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&r.x));
+            const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&r.y));
+            ss += lo.x * lo.x;
+            ss += lo.y * lo.y;
+            ss += hi.x * hi.x;
+            ss += hi.y * hi.y;
         }
         ss = warp_sum(ss);
-        if (lane == 0) sm.misc[m] = rsqrtf(ss / (float)a.d + a.eps);
+        if (lane == 0) wsum[wid * 8 + m] = ss;
+    }
+    __syncthreads();
+    if (threadIdx.x < a.B) {
+        float tot = 0.f;
+        for (int w = 0; w < kW; ++w) tot += wsum[w * 8 + threadIdx.x];
+        sm.misc[threadIdx.x] = rsqrtf(tot / (float)a.d + a.eps);
     }
     __syncthreads();
     // normalise in place: every thread rewrites the 4 values it read
-    const int nq = a.d / 4;
-    uint2 *xs = reinterpret_cast<uint2 *>(sm.work);
     for (int i = threadIdx.x; i < nq * a.B; i += kThreads) {
         const int m = i / nq, k = (i - m * nq) * 4;
         const uint2 r = xs[i];
