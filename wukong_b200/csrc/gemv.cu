@@ -648,18 +648,47 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         if (tid == 0) last = (atomicAdd(a.counter, 1) == (int)gridDim.x - 1);
         __syncthreads();
         if (last) {
+            // The best (value, key) is a maximum over a total order, so any
+            // reduction tree gives the same winner: 32 groups of 8 threads (one
+            // per activation row) take every 32nd CTA's partial, then the 4
+            // groups of a warp and the 8 warps are combined.
             __threadfence();
-            if (tid < a.M) {
-                float bv = -INFINITY;
-                uint64_t bk = ~0ull;
-                for (int b = 0; b < (int)gridDim.x; ++b) {
-                    const float ov = ((volatile float *)a.part_val)[(long)b * 8 + tid];
-                    const uint64_t ok = ((volatile unsigned long long *)a.part_key)[(long)b * 8 + tid];
-                    if (ov > bv || (ov == bv && ok < bk)) {
-                        bv = ov;
-                        bk = ok;
-                    }
+            const int mrow = tid & 7, grp = tid >> 3, wid = tid >> 5, lane = tid & 31;
+            float bv = -INFINITY;
+            uint64_t bk = ~0ull;
+            auto take = [&](float ov, uint64_t okey) {
+                if (ov > bv || (ov == bv && okey < bk)) {
+                    bv = ov;
+                    bk = okey;
                 }
+            };
+            for (int b0 = grp; b0 < (int)gridDim.x; b0 += 32 * 4) {
+                float ov[4];
+                uint64_t okey[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int b = b0 + u * 32;
+                    ov[u] = b < (int)gridDim.x ? __ldcg(a.part_val + (long)b * 8 + mrow) : -INFINITY;
+                    okey[u] = b < (int)gridDim.x ? __ldcg(a.part_key + (long)b * 8 + mrow) : ~0ull;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) take(ov[u], okey[u]);
+            }
+#pragma unroll
+            for (int o = 8; o < 32; o <<= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const uint64_t okey = __shfl_xor_sync(0xffffffffu, bk, o);
+                take(ov, okey);
+            }
+            if (lane < 8) {
+                sv[wid * 8 + lane] = bv;
+                sk[wid * 8 + lane] = bk;
+            }
+            __syncthreads();
+            if (tid < a.M) {
+                bv = -INFINITY;
+                bk = ~0ull;
+                for (int w = 0; w < kWarps; ++w) take(sv[w * 8 + tid], sk[w * 8 + tid]);
                 if (a.tokens) a.tokens[tid] = logits_index(bk, a.pack);
                 if (a.best_val) {
                     a.best_val[tid] = bv;
