@@ -204,6 +204,21 @@ __device__ __forceinline__ void mma16(float (&c)[4], uint32_t a0, uint32_t a1, u
         mma_f16(c, a0, a1, a2, a3, b0, b1);
 }
 
+// Q of a GQA group into shared memory [8][D], zero-padded to 8 heads, with
+// 16-byte loads (one round trip) when the row is 16-byte aligned
+template <typename T, int D>
+__device__ __forceinline__ void stage_q(T *qs, const T *qrow, int G) {
+    const int tid = threadIdx.x;
+    if ((reinterpret_cast<uintptr_t>(qrow) & 15) == 0) {
+        const int nv = G * D / 8;
+        for (int i = tid; i < D; i += 128)  // 8 heads x D / 8 uint4
+            reinterpret_cast<uint4 *>(qs)[i] =
+                i < nv ? reinterpret_cast<const uint4 *>(qrow)[i] : make_uint4(0u, 0u, 0u, 0u);
+    } else {
+        for (int i = tid; i < 8 * D; i += 128) qs[i] = i < G * D ? qrow[i] : from_float<T>(0.f);
+    }
+}
+
 template <typename T, int D, int S>
 __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out, long out_rs, const T *__restrict__ q,
                                                              long q_rs, const int *__restrict__ seq_of_row,
@@ -279,7 +294,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     }
     // Q of the group, zero-padded to 8 heads
     const T *qrow = q + (long)row * q_rs + (long)kvh * G * D;
-    for (int i = tid; i < 8 * D; i += 128) qs[i] = i < G * D ? qrow[i] : from_float<T>(0.f);
+    stage_q<T, D>(qs, qrow, G);
     __syncthreads();
     tl.phase(0);  // q staged
     uint32_t qb[D / 16][2];
@@ -501,7 +516,7 @@ __global__ void __launch_bounds__(128) attn_split_scores_kernel(const T *__restr
             bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
         }
     const T *qrow = q + (long)row * q_rs + (long)kvh * G * D;
-    for (int i = tid; i < 8 * D; i += 128) qs[i] = i < G * D ? qrow[i] : from_float<T>(0.f);
+    stage_q<T, D>(qs, qrow, G);
     __syncthreads();
     uint32_t qb[D / 16][2];
 #pragma unroll
