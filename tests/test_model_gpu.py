@@ -152,14 +152,15 @@ import wukong_b200 as wk
 from tests.model_util import LLAMA_1B, DeviceModel, host_mirror, make_weights
 L = wk.lib(); L.cuda_init(0)
 cfg = dict(LLAMA_1B); cfg["L"] = 2
-ctx = 80
+n_prompt, n_gen = int(sys.argv[2]), int(sys.argv[3])
+ctx = n_prompt + n_gen + 40
 w = make_weights(cfg, wk.Q8_0, wk.Q8_0, wk.F16, seed=21, ctx=ctx)
 dm = DeviceModel(w)
 h, _ = host_mirror(dm, cfg, wk.Q8_0, wk.Q8_0, wk.F16, ctx)
-prompt = np.random.default_rng(8).integers(0, cfg["V"], size=16).astype(np.int32)
-out = np.zeros(24, np.int32)
+prompt = np.random.default_rng(8).integers(0, cfg["V"], size=n_prompt).astype(np.int32)
+out = np.zeros(n_gen, np.int32)
 t0 = time.time()
-assert L.wk_host_llama_generate(h, prompt.ctypes.data_as(ctypes.c_void_p), 16, 24, out.ctypes.data_as(ctypes.c_void_p)) == 0
+assert L.wk_host_llama_generate(h, prompt.ctypes.data_as(ctypes.c_void_p), n_prompt, n_gen, out.ctypes.data_as(ctypes.c_void_p)) == 0
 dt = time.time() - t0
 # a second, different prompt sharing a prefix with the first
 p2 = np.concatenate([prompt[:9], np.array([5, 6, 7], np.int32)])
@@ -170,14 +171,17 @@ L.wk_host_llama_destroy(h); dm.free(); L.cuda_fini()
 """
 
 
-def test_prefix_cache_matches_full_recompute():
+@pytest.mark.parametrize("n_prompt,n_gen", [(16, 24), (520, 6)])
+def test_prefix_cache_matches_full_recompute(n_prompt, n_gen):
     """WUKONG_PREFIX_CACHE=1 turns model.go's re-prefill loop incremental; the greedy
-    tokens are those of the exact full recompute, also after the prompt changes."""
+    tokens are those of the exact full recompute, also after the prompt changes.
+    With a 520-token prompt (9 pages) the incremental decode splits each
+    (sequence, KV head) over CTAs (split-K attention)."""
     res = {}
     for flag in ("0", "1"):
         env = dict(os.environ, WUKONG_PREFIX_CACHE=flag)
-        r = subprocess.run([sys.executable, "-c", PREFIX_SCRIPT, ROOT], capture_output=True, text=True, env=env,
-                           timeout=600)
+        r = subprocess.run([sys.executable, "-c", PREFIX_SCRIPT, ROOT, str(n_prompt), str(n_gen)],
+                           capture_output=True, text=True, env=env, timeout=600)
         assert r.returncode == 0, r.stderr[-2000:]
         res[flag] = json.loads(r.stdout.strip().splitlines()[-1])
     assert res["1"]["tokens"] == res["0"]["tokens"]

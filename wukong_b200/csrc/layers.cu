@@ -57,6 +57,7 @@ struct Session {
     int *new_ids = nullptr;  // host copy of this pass's ids
     LayerKV layers[kMaxLayers];
     int nlayers = 0;
+    AttnSplitWs ws;  // split-K decode attention over the cached context (sized with the pools)
 };
 
 struct Shadow {
@@ -83,7 +84,33 @@ struct Carver {
     static size_t round(size_t n) { return (n + 255) & ~(size_t)255; }
 };
 
+void free_split_ws() {
+    AttnSplitWs &w = g_sess.ws;
+    for (void *p : {w.scores, (void *)w.mpart, (void *)w.opart, (void *)w.counter, (void *)w.minv})
+        if (p) WK_CHECK(cudaFreeAsync(p, stream()));
+    w = AttnSplitWs();
+}
+
+// split-K attention scratch for the session's sequences and `pages` pages each
+void alloc_split_ws(int pages) {
+    free_split_ws();
+    AttnSplitWs &w = g_sess.ws;
+    w.max_rows = g_sess.batch;
+    w.max_kv_heads = g_sess.kv_heads;
+    w.max_splits = 64;
+    w.lpad = pages * kPage;
+    const size_t rh = (size_t)g_sess.batch * g_sess.kv_heads;
+    WK_CHECK(cudaMallocAsync(&w.scores, rh * 8 * w.lpad * act_size(g_sess.act), stream()));
+    WK_CHECK(cudaMallocAsync((void **)&w.mpart, rh * w.max_splits * 16 * sizeof(float), stream()));
+    WK_CHECK(cudaMallocAsync((void **)&w.opart, rh * w.max_splits * 8 * g_sess.hd * sizeof(float), stream()));
+    WK_CHECK(cudaMallocAsync((void **)&w.counter, 2 * rh * sizeof(int), stream()));
+    WK_CHECK(cudaMemsetAsync(w.counter, 0, 2 * rh * sizeof(int), stream()));
+    w.counter_a = w.counter + rh;
+    WK_CHECK(cudaMallocAsync((void **)&w.minv, rh * 16 * sizeof(float), stream()));
+}
+
 void drop_session_layers() {
+    free_split_ws();
     for (int i = 0; i < g_sess.nlayers; ++i) {
         if (g_sess.layers[i].k) WK_CHECK(cudaFreeAsync(g_sess.layers[i].k, stream()));
         if (g_sess.layers[i].v) WK_CHECK(cudaFreeAsync(g_sess.layers[i].v, stream()));
@@ -127,6 +154,7 @@ void session_reserve(int rows) {
     WK_CHECK(cudaMallocAsync(&g_sess.block_table, sizeof(int) * g_sess.batch * np, stream()));
     fill_block_table(g_sess.block_table, g_sess.batch, np, stream());
     g_sess.max_pages = np;
+    alloc_split_ws(np);
 }
 
 LayerKV *session_layer(const void *qkv_w) {
@@ -257,12 +285,14 @@ void gqa_fused(void *out, const void *embeds, const float *freqs, const float *n
         a.kv_heads = kvNH;
         linear(a, rows, act, stream(), xn);
     }
+    // one new row per sequence over a cached context: long contexts split over CTAs
+    const AttnSplitWs *ws = r.cached && r.n == 1 && g_sess.ws.scores ? &g_sess.ws : nullptr;
     if (act == kF16)
         attention_paged<__half>((__half *)att, col, (const __half *)q, col, seq, pos, rows, row, kv, NH, stream(), true,
-                                nullptr, 0, r.n == 1);
+                                nullptr, 0, r.n == 1, ws);
     else
         attention_paged<__nv_bfloat16>((__nv_bfloat16 *)att, col, (const __nv_bfloat16 *)q, col, seq, pos, rows, row,
-                                       kv, NH, stream(), true, nullptr, 0, r.n == 1);
+                                       kv, NH, stream(), true, nullptr, 0, r.n == 1, ws);
     {
         GemvArgs a;
         a.w = (const uint8_t *)out_w;
