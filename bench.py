@@ -34,6 +34,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -78,8 +79,8 @@ class Clocks:
     def __init__(self, gpu):
         self.gpu = gpu
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "_work",
-                                 f"clocks_{os.getpid()}.csv")
+        out = os.path.join(ROOT, "gpurun_out")
+        self.path = os.path.join(out if os.path.isdir(out) else tempfile.gettempdir(), f"clocks_{os.getpid()}.csv")
 
     def __enter__(self):
         try:
@@ -89,7 +90,7 @@ class Clocks:
                 ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self
@@ -153,23 +154,43 @@ def run_ours(args, rank, world, local_rank):
     for _ in range(W):
         eng.step()
     torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+    # Every timed block decodes the same K steps: the sequences are rolled back
+    # to the block's start (wk_model_truncate) and get the same input ids again.
+    pos0 = L.wk_model_position(eng.m)
+    ids0 = np.zeros(B, np.int32)
+    L.cuda_to_host(ids0.ctypes.data_as(ctypes.c_void_p), L.wk_model_next_ids(eng.m), 4 * B)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local_rank) as clk:
+
+    def block():
+        wk.check(L.wk_model_truncate(eng.m, pos0))
+        L.cuda_to_device(L.wk_model_next_ids(eng.m), ids0.ctypes.data_as(ctypes.c_void_p), 4 * B)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(K):
             L.wk_model_decode_step(eng.m)
         e1.record(stream)
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
+        return e0.elapsed_time(e1)
+
+    def max_over_ranks(vals):
+        if world == 1:
+            return list(vals)
+        t = torch.tensor(vals, device="cuda", dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    res = dict(ms=ms, launches=eng.launches_per_step(), clocks=clk.summary(), tp=tpw,
-               step_bytes=sm.weight_bytes_per_step() + kv_bytes(cfg, P + W + K // 2, B, tpw))
+        return t.tolist()
+
+    # enough identical blocks for the clock sampler to see seconds of load
+    first = max_over_ranks([block()])[0]
+    R = int(min(args.max_blocks, max(args.min_blocks, -(-args.timed_seconds * 1e3 // first))))
+    with Clocks(local_rank) as clk:
+        times = [block() for _ in range(R)]
+    times = max_over_ranks(times)
+    ms = statistics.median(times)
+    res = dict(ms=ms, blocks=R, block_ms_min=min(times), block_ms_max=max(times), launches=eng.launches_per_step(),
+               clocks=clk.summary(), tp=tpw, step_bytes=sm.weight_bytes_per_step() + kv_bytes(cfg, pos0 + K // 2, B, tpw))
 
     # dominant kernel: the Q8_0 dequant-GEMV at the FFN up|gate shape of the
     # model (per rank), timed alone over 8 rotating weight copies (> L2)
@@ -331,6 +352,9 @@ def run_cpu(model, B, P, steps, budget_s=25.0):
     from wukong_b200.engine import LLAMA
     cfg = dict(LLAMA[model])
     orc.set_threads(os.cpu_count() or 1)
+    # 8B: a 128-token prompt instead of 2048 keeps the CPU prefill to seconds;
+    # a decode step there is bound by the 8 GB of weights, not by the context
+    P_full, P = P, (P if model == "1b" else min(P, 128))
     w = make_weights(cfg, 8, 8, 1, seed=SEED, ctx=P + steps + 16)
     om = oracle_model(w, cfg, 8, 8, 1, P + steps + 16)
     om.reset(B)
@@ -343,7 +367,8 @@ def run_cpu(model, B, P, steps, budget_s=25.0):
         n += 1
     dt = time.perf_counter() - t0
     return dict(value=B * n / dt, unit="tokens/s", cores=orc.num_threads(), kind="port",
-                sample=f"{n} decode steps after a {P}-token prefill, batch {B}, {NAMES[model]} Q8_0")
+                sample=f"{n} decode steps after a {P}-token prefill, batch {B}, {NAMES[model]} Q8_0"
+                       + ("" if P == P_full else f" (the GPU arm's prompt is {P_full} tokens)"))
 
 
 # ------------------------------------------------------------------ main
@@ -353,7 +378,13 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--model", default="1b", choices=["1b", "8b", "70b"])
+    ap.add_argument("--model", default=None, choices=["1b", "8b", "70b"],
+                    help="default: 1b on one plain process; 8b (tensor-parallel over the ranks) under "
+                         "torch.distributed.run, at every world size including 1")
+    ap.add_argument("--min-blocks", type=int, default=20, help="timed blocks of --steps steps (at least)")
+    ap.add_argument("--max-blocks", type=int, default=400)
+    ap.add_argument("--timed-seconds", type=float, default=3.0,
+                    help="blocks are added until about this much decode time is timed")
     ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 128 / 2048 / 4096)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
@@ -363,11 +394,17 @@ def main():
                          "e.g. 8192x2048x1,8192x2048x16,8192x2048x128")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.prompt is None:
-        args.prompt = PROMPTS[args.model]
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.model is None:
+        # the multi-GPU curve is tensor-parallel Llama-3.1-8B decode at every N
+        # (N = 1 included when launched by torch.distributed.run); one plain
+        # process measures the single-GPU headline, Llama-3.2-1B
+        launched = "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_WORLD_SIZE" in os.environ
+        args.model = "8b" if (launched or world > 1 or args.gpus > 1) else "1b"
+    if args.prompt is None:
+        args.prompt = PROMPTS[args.model]
     tp = args.model != "1b" and world > 1
     if tp:
         par = f"tp{world}"
@@ -379,7 +416,9 @@ def main():
               "model": NAMES[args.model], "batch": args.batch, "prompt": args.prompt, "decode_steps": args.steps,
               "weights": "Q8_0 linear layers and output.weight, token_embd F16, norms 1.0, w ~ N(0, 0.02), "
                          "generated on the device",
-              "l2": "weights read per step exceed the 126 MB L2, no flush", "parallelism": par}
+              "l2": "weights read per step exceed the 126 MB L2, no flush", "parallelism": par,
+              "timing": f"median of identical timed blocks of {args.steps} decode steps, each from the same "
+                        "position with the same ids (max over ranks per block)"}
 
     if args.op:
         run_op(args.op)
@@ -387,6 +426,10 @@ def main():
 
     if args.impl == "reference":
         if rank != 0:
+            return
+        if args.model == "70b":
+            print(json.dumps({"impl": "reference", "unavailable": "the 70B CPU restatement needs about 80 GB of "
+                              "host memory for its weights; no CPU run at this size"}))
             return
         cpu = run_cpu(args.model, args.batch, args.prompt, args.warmup + args.steps, budget_s=150.0)
         line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "n_gpus": 1,
@@ -419,7 +462,9 @@ def main():
     step_gbs = res["step_bytes"] / (res["ms"] / K) / 1e6
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
-        "ms_per_step": res["ms"] / K, "higher_is_better": True, "scaling": "strong" if tp else "weak",
+        "ms_per_step": res["ms"] / K, "timed_blocks": res["blocks"],
+        "block_ms": {"median": res["ms"], "min": res["block_ms_min"], "max": res["block_ms_max"]},
+        "higher_is_better": True, "scaling": "strong" if tp else "weak",
         "vs_baseline": None, "dtype": "int8 x f16 -> f32", "data": "synthetic", "config": config,
         "gpu_launches": res["launches"] * K,
         "roofline": {"bound": "hbm", "kernel": f"gemv_kernel<Q8_0> {g['N']}x{g['K']} M={g['M']}",

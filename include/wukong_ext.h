@@ -61,6 +61,11 @@ int *wk_model_next_ids(wk_model *m);
 int wk_model_step_launches(const wk_model *m);
 /* current sequence length (positions used) */
 int wk_model_position(const wk_model *m);
+/* Roll every armed sequence back to n positions (1 <= n <= current length):
+ * the next decode step writes position n again, overwriting the cached K/V
+ * from there on.  The next input ids (wk_model_next_ids) are left as they are;
+ * the caller sets them.  Used to discard speculative or timed continuations. */
+int wk_model_truncate(wk_model *m, int n);
 
 /* Synthetic weights, bit-identical to the CPU oracle's generator:
  * Irwin-Hall(4) normal(0, stdv) samples of a counter-based hash. */
@@ -97,6 +102,20 @@ int wk_tp_world(void);
  * (WUKONG_TP_P2P=0, or a rank could not map the others' buffers) */
 int wk_tp_p2p(void);
 int wk_model_set_tp(wk_model *m, int enable);
+/* The exchange of wk_tp_p2p on this one GPU, for testing the failure path:
+ * ranks 1..world-1 are emulated by buffers on this device.  publish = 1 writes
+ * their partial sums and flags first, so the exchange completes and its sum is
+ * checked; publish = 0 leaves them unwritten, so every CTA's bounded wait runs
+ * out (after WUKONG_WAIT_LIMIT_MS, read at cuda_init; default 1000) and
+ * records code 40 in the device error word.  Returns the error word after the
+ * launch (0: completed), -2 for a wrong sum, -1 for a setup error.  Does not
+ * need wk_tp_init. */
+int wk_tp_exchange_selftest(int world, int publish);
+/* The device error word: the code of the first bounded device wait that gave
+ * up since it was last cleared (0: none), after synchronising the library
+ * stream; clear = 1 resets it.  cuda_to_host ends the process when it is set,
+ * and wk_model_prefill / wk_model_decode_step refuse to launch (return -1). */
+int wk_device_error(int clear);
 
 /* No counterpart in the reference.  cuda_predict without device allocation,
  * for hosts that cannot call cudaMalloc at that point: a process that has
@@ -107,10 +126,12 @@ int wk_model_set_tp(wk_model *m, int enable);
  * output weights, same kernel.  Its scratch is a fixed 393,472-byte array
  * inside the library (every GPU that loads the library holds it until exit),
  * so a call takes at most 64 sequences and col <= 32768; larger or unsupported
- * sizes return -1 with the reason in wk_last_error().  All calls share that
- * array: calls that overlap on the GPU race; calls on the library stream do
- * not.  The first call on a device looks up the array's address; make it
- * before any stream capture.  Returns 0 on success. */
+ * sizes return -1 with the reason in wk_last_error().  CUDA errors inside the
+ * GEMV launch end the process with a message, as cuda_predict's do.  All calls
+ * share that array: calls that overlap on the GPU race; calls on the library
+ * stream do not.  The first call on a device looks up the array's address
+ * (cached until cuda_fini); make it before any stream capture.  Returns 0 on
+ * success. */
 int wk_predict_noalloc(int *out, const void *ff, const void *norm_weight, const void *out_weight, int batch,
                        int row, int col, int wsize, float eps, int dtype);
 

@@ -8,7 +8,9 @@ Nothing from the reference is executed.
 
 Usage (in a checkout that has the reference sources mounted):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference checkout>
+
+(default: $WUKONG_REFERENCE_SRC, else /root/reference)
 
 The JSON maps ``"<suite>/<test>" -> {"<array name>": [values...]}``.  For Go
 tests that build tensors inline (``x, err := MakeTensorErr(Shape{..}, []float32{..})``)
@@ -102,4 +104,4 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("WUKONG_REFERENCE_SRC", "/root/reference"))

@@ -5,7 +5,10 @@ wukong_b200.tp, join one NCCL communicator through wk_tp_init and run prefill
 (tcgen05 GEMM path, 48 rows) and greedy decode steps (GEMV path) with the
 row-parallel partial sums, the fp32 all-reduce and the vocabulary-parallel
 argmax exchange.  Their tokens must equal those of the unsharded engine on the
-same weights.  Skipped on a box with fewer than 2 GPUs.
+same weights.  A second test shards one layer at Llama-3.1-8B widths (head_dim
+128, d 4096, FFN 14336, vocabulary 128256) and checks the ranks' tokens
+against the CPU oracle, teacher-forced.  Skipped on a box with fewer than 2
+GPUs.
 """
 import ctypes
 import os
@@ -116,3 +119,101 @@ def test_tp2_engine_matches_single_gpu(dev, p2p):
     assert used0 == used1 == int(p2p)
     assert t0 == t1
     assert t0 == ref
+
+
+# ------------------------------------------------------------------ 8B widths vs the oracle
+CFG8 = dict(L=1, d=4096, H=32, Hk=8, D=128, F=14336, V=128256, eps=1e-5, theta=500000.0)
+B8, P8, STEPS8, CTX8 = 2, 40, 6, 64
+
+
+def _model8():
+    from tests.model_util import make_weights
+    return make_weights(CFG8, wk.Q8_0, wk.Q8_0, wk.F16, seed=8080, ctx=CTX8)
+
+
+def _worker8(rank, world, uid, q, prompt, forced):
+    """Prefill, then one decode step per oracle token (teacher forcing)."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        from tests.gpu_util import down, up
+        from wukong_b200 import tp
+        from wukong_b200.engine import Engine
+        L = wk.lib()
+        L.cuda_init(rank)
+        wk.check(L.wk_tp_init(rank, world, uid))
+        w = _model8()
+        layers = []
+        for lw in w["layers"]:
+            s = tp.shard_layer(lw, CFG8, wk.Q8_0, rank, world)
+            layers.append({k: up(v) for k, v in s.items()})
+        out = up(tp.shard_output(w["output"], CFG8, wk.Q8_0, rank, world))
+        ptrs = [up(w["token_embd"]), up(w["output_norm"]), up(w["freqs"])]
+        eng = Engine(tp.local_config(CFG8, world), layers, ptrs[0], ptrs[1], out, ptrs[2], CTX8, max_batch=B8,
+                     tp=True)
+        dp = up(prompt)
+        eng.prefill(dp, B8, P8)
+        toks = [down(eng.tokens_ptr(), B8, np.int32).tolist()]
+        for f in forced:
+            fa = np.ascontiguousarray(f, np.int32)
+            L.cuda_to_device(L.wk_model_next_ids(eng.m), fa.ctypes.data_as(ctypes.c_void_p), 4 * B8)
+            eng.step()
+            toks.append(down(eng.tokens_ptr(), B8, np.int32).tolist())
+        eng.destroy()
+        L.wk_tp_fini()
+        q.put((rank, toks))
+    except Exception as e:  # reported to the parent
+        q.put((rank, f"{type(e).__name__}: {e}"))
+
+
+def test_tp2_8b_widths_vs_oracle(dev):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs 2 GPUs")
+    import queue
+    import time
+    import torch.multiprocessing as mp
+    from tests.model_util import oracle_model
+    w = _model8()
+    prompt = np.random.default_rng(88).integers(0, CFG8["V"], size=(B8, P8)).astype(np.int32)
+    om = oracle_model(w, CFG8, wk.Q8_0, wk.Q8_0, wk.F16, CTX8)
+    om.reset(B8)
+    tok, logits, _ = om.forward(prompt)
+    ref, lgs = [tok.tolist()], [logits]
+    for _ in range(STEPS8):
+        tok, logits, _ = om.forward(tok.reshape(B8, 1))
+        ref.append(tok.tolist())
+        lgs.append(logits)
+    uid = ctypes.create_string_buffer(128)
+    wk.check(dev.wk_tp_unique_id(uid))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker8, args=(r, 2, uid.raw, q, prompt, ref[:-1])) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        t0 = time.time()
+        while len(got) < 2 and time.time() - t0 < 300:
+            try:
+                r, v = q.get(timeout=2)
+                got[r] = v
+            except queue.Empty:
+                if any(p.exitcode not in (None, 0) for p in procs) and q.empty():
+                    break
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert set(got) == {0, 1}, f"ranks reported {sorted(got)}; exit codes {[p.exitcode for p in procs]}"
+    assert isinstance(got[0], list), got[0]
+    assert got[0] == got[1]
+    ties = []
+    for s, (g, r, lg) in enumerate(zip(got[0], ref, lgs)):
+        for b in range(B8):
+            if g[b] != r[b]:
+                scale = float(np.abs(lg[b]).max())
+                mg = abs(float(lg[b][g[b]]) - float(lg[b][r[b]]))
+                assert mg <= 2 * 2.0 ** -10 * scale, (s, b, g[b], r[b], mg)
+                ties.append((s, b, mg))
+    assert len(ties) <= 1, ties

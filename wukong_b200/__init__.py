@@ -65,6 +65,7 @@ EXT = {
     "wk_model_next_ids": (_P, [_P]),
     "wk_model_step_launches": (_I, [_P]),
     "wk_model_position": (_I, [_P]),
+    "wk_model_truncate": (_I, [_P, _I]),
     "wk_fill_random_q8_0": (_I, [_P, _L, _I, _U64, _F]),
     "wk_fill_random_f16": (_I, [_P, _L, _U64, _F]),
     "wk_fill_const_f32": (_I, [_P, _L, _F]),
@@ -80,6 +81,8 @@ EXT = {
     "wk_tp_world": (_I, []),
     "wk_tp_p2p": (_I, []),
     "wk_model_set_tp": (_I, [_P, _I]),
+    "wk_tp_exchange_selftest": (_I, [_I, _I]),
+    "wk_device_error": (_I, [_I]),
 }
 
 

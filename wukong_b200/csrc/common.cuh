@@ -70,6 +70,12 @@ struct Runtime {
     bool pdl = true;      // programmatic dependent launch on the hot kernels
     bool tc_gemm = true;  // tcgen05 GEMM for activation blocks of >= 16 rows
     int warp_tile_min = 4096;  // SwiGLU / logits layers with this many 16-row tiles run one tile per warp
+    // limit of the cross-GPU flag waits of the tensor-parallel exchange
+    // (WUKONG_WAIT_LIMIT_MS, default one second)
+    unsigned long long wait_limit_ns = 1000000000ull;
+    // called by cuda_fini with the device index (set by parts that cache
+    // per-device state; a pointer, so cuda.h's objects do not link them in)
+    void (*on_fini)(int device) = nullptr;
 };
 extern Runtime g_rt;
 

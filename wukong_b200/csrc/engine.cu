@@ -666,8 +666,18 @@ int wk_model_set_tp(wk_model *m, int enable) {
     return 0;
 }
 
+// A bounded device wait that gave up (a lost peer, a copy that never landed)
+// left the decode state incomplete: refuse further launches until the host
+// has handled it (wk_device_error).  Tensor-parallel ranks are then out of
+// step; recovery is wk_tp_fini and a new communicator.
+static int device_error_pending() {
+    const int e = g_rt.h_error ? *(volatile int *)g_rt.h_error : 0;
+    return e ? fail("a device-side bounded wait gave up earlier (code %d); see wk_device_error", e) : 0;
+}
+
 int wk_model_prefill(wk_model *m, const int *ids, int batch, int n, int *tokens_out) {
     if (!m || !m->kpool) return fail("cache not allocated");
+    if (device_error_pending()) return -1;
     if (batch <= 0 || batch > m->max_batch || n <= 0 || n > m->max_ctx || n > m->freqs_ctx)
         return fail("prefill batch %d x %d exceeds the cache (%d x %d)", batch, n, m->max_batch, m->max_ctx);
     set_device_current();
@@ -694,6 +704,7 @@ int wk_model_prefill(wk_model *m, const int *ids, int batch, int n, int *tokens_
 int wk_model_decode_step(wk_model *m) {
     if (!m || m->batch <= 0) return fail("no armed batch (call wk_model_prefill first)");
     if (m->pos + 1 > m->max_ctx || m->pos + 1 > m->freqs_ctx) return fail("context full (%d)", m->pos);
+    if (device_error_pending()) return -1;
     set_device_current();
     cudaStream_t s = stream();
     const int B = m->batch;
@@ -750,6 +761,17 @@ const int *wk_model_tokens(const wk_model *m) { return m ? m->d_tokens : nullptr
 int *wk_model_next_ids(wk_model *m) { return m ? m->d_ids : nullptr; }
 int wk_model_step_launches(const wk_model *m) { return m ? m->step_launches : 0; }
 int wk_model_position(const wk_model *m) { return m ? m->pos : 0; }
+
+int wk_model_truncate(wk_model *m, int n) {
+    if (!m || m->batch <= 0) return fail("no armed batch (call wk_model_prefill first)");
+    if (n < 1 || n > m->pos) return fail("truncate to %d outside [1, %d]", n, m->pos);
+    set_device_current();
+    cudaStream_t s = stream();
+    fill_i32_kernel<<<(m->batch + 127) / 128, 128, 0, s>>>(m->d_pos, m->batch, n);
+    WK_TRY(cudaGetLastError());
+    m->pos = n;
+    return 0;
+}
 
 int wk_fill_random_q8_0(void *dst, long rows, int cols, uint64_t seed, float stdv) {
     if (cols % 32) return fail("cols must be a multiple of 32");

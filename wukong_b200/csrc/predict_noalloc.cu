@@ -68,6 +68,12 @@ __global__ void clear_counters_kernel(int passes) {
 constexpr int kMaxDevices = 64;
 std::atomic<unsigned char *> g_scratch_addr[kMaxDevices];
 
+// cuda_fini drops the cached address: after a new cuda_init (which may follow a
+// reset of the device's context) the first call looks it up again.
+void forget_address(int device) {
+    if (device >= 0 && device < kMaxDevices) g_scratch_addr[device].store(nullptr, std::memory_order_release);
+}
+
 // Device address of g_predict_scratch on the current device, looked up once
 // per device (the first call on each device does it).
 unsigned char *scratch_address(int device) {
@@ -81,6 +87,7 @@ unsigned char *scratch_address(int device) {
         return nullptr;
     }
     g_scratch_addr[device].store((unsigned char *)addr, std::memory_order_release);
+    g_rt.on_fini = forget_address;
     return (unsigned char *)addr;
 }
 

@@ -93,6 +93,8 @@ void cuda_init(int idx) {
     g_rt.tc_gemm = !(tc && tc[0] == '0');
     const char *wt = getenv("WUKONG_WARP_TILE_MIN");
     if (wt && atoi(wt) > 0) g_rt.warp_tile_min = atoi(wt);
+    const char *wl = getenv("WUKONG_WAIT_LIMIT_MS");
+    if (wl && atoi(wl) > 0) g_rt.wait_limit_ns = 1000000ull * (unsigned long long)atoi(wl);
     printf("Running on GPU %d: %s, Compute Capability %d.%d\n", idx, prop.name, prop.major, prop.minor);
     fflush(stdout);
     layers_init();
@@ -104,6 +106,7 @@ void cuda_fini(void) {
     set_device_current();
     layers_fini();
     WK_CHECK(cudaStreamSynchronize(g_rt.stream));
+    if (g_rt.on_fini) g_rt.on_fini(g_rt.device);
     if (g_rt.ws) WK_CHECK(cudaFree(g_rt.ws));
     g_rt.ws = nullptr;
     g_rt.ws_size = 0;
@@ -145,6 +148,15 @@ void cuda_to_host(void *dst, void *src, size_t size) {
     WK_CHECK(cudaMemcpyAsync(dst, src, size, cudaMemcpyDeviceToHost, g_rt.stream));
     WK_CHECK(cudaStreamSynchronize(g_rt.stream));
     check_device_error();
+}
+
+int wk_device_error(int clear) {
+    if (g_rt.device < 0 || !g_rt.h_error) return 0;
+    set_device_current();
+    WK_CHECK(cudaStreamSynchronize(g_rt.stream));
+    const int e = *(volatile int *)g_rt.h_error;
+    if (clear) *(volatile int *)g_rt.h_error = 0;
+    return e;
 }
 
 // cuda.cu:1267-1275: row concatenation of two tensors of the same dtype.

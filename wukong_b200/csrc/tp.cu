@@ -17,6 +17,8 @@
 #include <nccl.h>  // types only; every function is resolved with dlsym
 #include <string.h>
 
+#include <vector>
+
 #include "common.cuh"
 #include "wukong_ext.h"
 #include "wukong_internal.cuh"
@@ -123,12 +125,13 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-// Wait until *flag == e; false (error recorded) after one second.
-__device__ bool wait_flag(const unsigned long long *flag, unsigned long long e, int *err, int code) {
+// Wait until *flag >= e; false (error recorded) after limit_ns.
+__device__ bool wait_flag(const unsigned long long *flag, unsigned long long e, int *err, int code,
+                          unsigned long long limit_ns) {
     if (ld_acquire_sys(flag) >= e) return true;
     const uint64_t t0 = globaltimer_ns();
     while (ld_acquire_sys(flag) < e) {
-        if (globaltimer_ns() - t0 > 1000000000ull) {
+        if (globaltimer_ns() - t0 > limit_ns) {
             atomicCAS(err, 0, code);
             return false;
         }
@@ -141,7 +144,8 @@ __device__ bool wait_flag(const unsigned long long *flag, unsigned long long e, 
 template <typename T>
 __global__ void __launch_bounds__(512) p2p_allreduce_resid_kernel(T *__restrict__ x, const float *__restrict__ partial,
                                                                   long n, uint8_t *const *peers, int rank, int world,
-                                                                  unsigned long long *epochs, int *err) {
+                                                                  unsigned long long *epochs, int *err,
+                                                                  unsigned long long limit_ns) {
     __shared__ unsigned long long e_s;
     __shared__ int ok_s;
     const int c = blockIdx.x, tid = threadIdx.x;
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(512) p2p_allreduce_resid_kernel(T *__restrict_
         st_release_sys(reinterpret_cast<unsigned long long *>(peers[rank]) + par * kArCtas + c, e);
     }
     if (tid < world && !wait_flag(reinterpret_cast<const unsigned long long *>(peers[tid]) + par * kArCtas + c, e,
-                                  err, 40))
+                                  err, 40, limit_ns))
         ok_s = 0;
     __syncthreads();
     if (!ok_s) return;
@@ -177,7 +181,8 @@ __global__ void __launch_bounds__(512) p2p_allreduce_resid_kernel(T *__restrict_
 // Logits winners: keys [B] u64 and values [B] f32 of every rank -> token ids.
 __global__ void __launch_bounds__(32) p2p_argmax_kernel(int *__restrict__ tokens, const uint8_t *__restrict__ send, int B,
                                                         int pack, uint8_t *const *peers, int rank, int world,
-                                                        unsigned long long *epochs, int *err) {
+                                                        unsigned long long *epochs, int *err,
+                                                        unsigned long long limit_ns) {
     __shared__ unsigned long long e_s;
     __shared__ int ok_s;
     const int tid = threadIdx.x;
@@ -197,7 +202,8 @@ __global__ void __launch_bounds__(32) p2p_argmax_kernel(int *__restrict__ tokens
         __threadfence_system();
         st_release_sys(reinterpret_cast<unsigned long long *>(peers[rank] + 256) + par, e);
     }
-    if (tid < world && !wait_flag(reinterpret_cast<const unsigned long long *>(peers[tid] + 256) + par, e, err, 41))
+    if (tid < world &&
+        !wait_flag(reinterpret_cast<const unsigned long long *>(peers[tid] + 256) + par, e, err, 41, limit_ns))
         ok_s = 0;
     __syncthreads();
     if (!ok_s) return;
@@ -302,7 +308,7 @@ void tp_argmax_combine(int *tokens, const void *send, void *recv, int B, int pac
     const size_t chunk = tp_winner_chunk(B);
     if (g_p2p.ok && chunk <= kWinSlot) {
         p2p_argmax_kernel<<<1, 32, 0, s>>>(tokens, (const uint8_t *)send, B, pack, g_p2p.peers_d, g_rank, g_world,
-                                           g_p2p.epochs, g_rt.d_error);
+                                           g_p2p.epochs, g_rt.d_error, g_rt.wait_limit_ns);
         WK_CHECK_LAUNCH();
         return;
     }
@@ -318,7 +324,7 @@ template <typename T> int allreduce_resid(T *x, float *p, long n, cudaStream_t s
         // always kArCtas CTAs: every CTA index takes part in every call, so all
         // CTAs of a call use the same slot parity (see the layout comment)
         p2p_allreduce_resid_kernel<T><<<kArCtas, 512, 0, s>>>(x, p, n, g_p2p.peers_d, g_rank, g_world, g_p2p.epochs,
-                                                           g_rt.d_error);
+                                                           g_rt.d_error, g_rt.wait_limit_ns);
         WK_CHECK_LAUNCH();
         return 1;
     }
@@ -381,6 +387,67 @@ void wk_tp_fini(void) {
     g_comm = nullptr;
     g_rank = 0;
     g_world = 1;
+}
+
+int wk_tp_exchange_selftest(int world, int publish) {
+    if (g_rt.device < 0) return fail("wk_tp_exchange_selftest: cuda_init() has not been called");
+    if (world < 2 || world > kMaxWorld) return fail("wk_tp_exchange_selftest: world %d outside [2, %d]", world, kMaxWorld);
+    set_device_current();
+    cudaStream_t s = stream();
+    const long n = 4096;  // one decode row of an 8B model
+    uint8_t *bufs[kMaxWorld] = {};
+    uint8_t **peers_d = nullptr;
+    unsigned long long *epochs = nullptr;
+    __half *x = nullptr;
+    float *partial = nullptr;
+    int rc = 0;
+    auto ok = [&](cudaError_t e) {
+        if (e != cudaSuccess && rc == 0) rc = fail("wk_tp_exchange_selftest: %s", cudaGetErrorString(e));
+        return rc == 0;
+    };
+    for (int r = 0; r < world && ok(cudaMalloc(&bufs[r], kP2PBytes)); ++r) ok(cudaMemset(bufs[r], 0, kP2PBytes));
+    ok(cudaMalloc(&peers_d, sizeof(uint8_t *) * kMaxWorld)) &&
+        ok(cudaMemcpy(peers_d, bufs, sizeof(uint8_t *) * kMaxWorld, cudaMemcpyHostToDevice));
+    ok(cudaMalloc(&epochs, sizeof(unsigned long long) * (kArCtas + 1))) &&
+        ok(cudaMemset(epochs, 0, sizeof(unsigned long long) * (kArCtas + 1)));
+    ok(cudaMalloc(&x, sizeof(__half) * n)) && ok(cudaMalloc(&partial, sizeof(float) * n));
+    if (rc == 0) {
+        std::vector<__half> hx(n, __float2half(1.0f));
+        std::vector<float> hp(n, 1.0f);
+        ok(cudaMemcpy(x, hx.data(), sizeof(__half) * n, cudaMemcpyHostToDevice));
+        ok(cudaMemcpy(partial, hp.data(), sizeof(float) * n, cudaMemcpyHostToDevice));
+        if (publish) {
+            // the emulated ranks' first call (epoch 1, slot parity 1): partials of 1.0 and every CTA's flag
+            std::vector<unsigned long long> flags(kArCtas, 1ull);
+            for (int r = 1; r < world; ++r) {
+                ok(cudaMemcpy(bufs[r] + kP2POff + kArSlot, hp.data(), sizeof(float) * n, cudaMemcpyHostToDevice));
+                ok(cudaMemcpy(reinterpret_cast<unsigned long long *>(bufs[r]) + kArCtas, flags.data(),
+                              sizeof(unsigned long long) * kArCtas, cudaMemcpyHostToDevice));
+            }
+        }
+    }
+    if (rc == 0) {
+        ok(cudaStreamSynchronize(s));
+        p2p_allreduce_resid_kernel<__half><<<kArCtas, 512, 0, s>>>(x, partial, n, peers_d, 0, world, epochs,
+                                                                g_rt.d_error, g_rt.wait_limit_ns);
+        ok(cudaGetLastError()) && ok(cudaStreamSynchronize(s));
+    }
+    if (rc == 0) {
+        rc = *(volatile int *)g_rt.h_error;
+        if (rc == 0) {
+            // x = T(1 + T(world * 1.0))
+            std::vector<__half> hx(n);
+            ok(cudaMemcpy(hx.data(), x, sizeof(__half) * n, cudaMemcpyDeviceToHost));
+            for (long i = 0; rc == 0 && i < n; ++i)
+                if (__half2float(hx[i]) != 1.0f + (float)world) rc = -2;
+            if (rc == -2) fail("wk_tp_exchange_selftest: wrong sum");
+        }
+    }
+    for (int r = 0; r < world; ++r)
+        if (bufs[r]) cudaFree(bufs[r]);
+    for (void *p : {(void *)peers_d, (void *)epochs, (void *)x, (void *)partial})
+        if (p) cudaFree(p);
+    return rc;
 }
 
 int wk_tp_rank(void) { return g_rank; }
