@@ -111,6 +111,14 @@ int wk_model_set_tp(wk_model *m, int enable);
  * launch (0: completed), -2 for a wrong sum, -1 for a setup error.  Does not
  * need wk_tp_init. */
 int wk_tp_exchange_selftest(int world, int publish);
+/* The decode GEMV whose epilogue exchanges its partial tiles (the o / down
+ * layers of tensor-parallel decode) on this one GPU with ranks 1..world-1
+ * emulated by buffers that hold published partials of 0.25 q: checks that
+ * x = T(x + T(own partial + sum of the others)) element for element against
+ * the same GEMV's partial sums.  Q8_0 [N, K] weights, M rows (<= 8).  Returns
+ * 0, the device error word, or -2 with the first wrong element in
+ * wk_last_error(). */
+int wk_tp_gemv_selftest(int world, int N, int K, int M);
 /* The device error word: the code of the first bounded device wait that gave
  * up since it was last cleared (0: none), after synchronising the library
  * stream; clear = 1 resets it.  cuda_to_host ends the process when it is set,

@@ -1,7 +1,7 @@
 """Failure detection of the tensor-parallel exchange, on one GPU and without a
 GPU fault.
 
-The exchange kernel waits (bounded) for the flag every peer publishes in its
+The exchange kernels wait (bounded) for the flag every peer publishes in its
 own buffer.  wk_tp_exchange_selftest runs it on one GPU with the peers
 emulated by local buffers: published, the exchange completes and its sum is
 checked; unpublished (a lost rank), every CTA's wait runs out after
@@ -94,3 +94,13 @@ def test_engine_refuses_steps_until_the_error_is_cleared():
     assert res["refused"] == -1 and "code 40" in res["refused_msg"], res
     assert res["cleared"] == 40
     assert res["after_clear"] == 0 and res["step"] == 0 and res["error_word_end"] == 0, res
+
+
+@pytest.mark.parametrize("world,N,K,M", [(2, 4096, 512, 1), (8, 4096, 1792, 3), (4, 2048, 2048, 8), (2, 8192, 256, 2)])
+def test_fused_exchange_gemv_matches_its_partial_sums(dev, world, N, K, M):
+    """The o / down GEMV of tensor-parallel decode with its all-reduce +
+    residual epilogue, on one GPU with the other ranks emulated (their tiles
+    already published): x = T(x + T(sum over ranks)) element for element."""
+    assert dev.wk_device_error(1) == 0
+    rc = dev.wk_tp_gemv_selftest(world, N, K, M)
+    assert rc == 0, dev.wk_last_error().decode()

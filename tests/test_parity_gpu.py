@@ -2,10 +2,11 @@
 reference's own cuda.cu at the shapes of the benchmark configurations:
 
 * Llama-3.2-1B at full depth (16 layers, Q8_0, batch 1, 128-token prompt),
-  256 free-running greedy steps: the token sequence must be identical to the
-  oracle's and to the reference cuda.cu's (driven through the reference's Go
-  call sequence, llm/model.go:116-178, by the C++ host mirror).  A mismatch
-  fails the test and reports the step and the oracle's top-2 logit margin.
+  256 greedy steps with the engine feeding its own tokens back: identical to
+  the oracle's tokens at every step except where the oracle's two best logits
+  tie in fp16, which are listed with their margins; the reference's own
+  cuda.cu (through the reference's Go call sequence, llm/model.go:116-178, in
+  the C++ host mirror) is held to the same rule.
 * Llama-3.1-8B widths (head_dim 128, d 4096, FFN 14336, vocabulary 128256),
   one and two layers, contexts of 40 and 520 tokens (the second splits the
   attention over CTAs), against the oracle.
@@ -91,27 +92,42 @@ def llama_1b_full(dev):
     om = oracle_model(w, cfg, wk.Q8_0, wk.Q8_0, wk.F16, ctx)
     om.reset(1)
     tok, logits, _ = om.forward(prompt)
-    seq, margins = [int(tok[0])], [top2_margin(logits[0])[0]]
+    seq, lgs = [int(tok[0])], [logits[0].copy()]
     for _ in range(STEPS_256):
         tok, logits, _ = om.forward(tok.reshape(1, 1))
         seq.append(int(tok[0]))
-        margins.append(top2_margin(logits[0])[0])
-    yield dict(cfg=cfg, ctx=ctx, w=w, dm=dm, prompt=prompt, oracle=seq, margins=margins)
+        lgs.append(logits[0].copy())
+    margins = [top2_margin(l)[0] for l in lgs]
+    ties = [i for i, l in enumerate(lgs) if margins[i] <= 2 * 2.0 ** -10 * float(np.abs(l).max())]
+    print(f"1B oracle, {STEPS_256 + 1} greedy tokens ({len(set(seq))} distinct): steps whose top-2 logits are "
+          f"within two fp16 rounding steps of the logit scale: {[(i, round(margins[i], 6)) for i in ties]}")
+    yield dict(cfg=cfg, ctx=ctx, w=w, dm=dm, prompt=prompt, oracle=seq, logits=lgs, margins=margins, ties=ties)
     dm.free()
 
 
-def _first_mismatch(a, b):
-    for i, (x, y) in enumerate(zip(a, b)):
-        if x != y:
-            return i
-    return None
+def _check_sequence(got, t, who):
+    """got[i] is the token produced at step i.  Identical to the oracle's except
+    at its fp16 near-ties, where it must be one of the tied best tokens."""
+    div = [i for i, (g, r) in enumerate(zip(got, t["oracle"])) if g != r]
+    for i in div:
+        lg = t["logits"][i]
+        assert near_tie(lg, got[i], t["oracle"][i]), (
+            f"{who} token {i} is {got[i]}, the oracle's {t['oracle'][i]}: not a near-tie (oracle logits "
+            f"{float(lg[got[i]]):.6f} vs {float(lg[t['oracle'][i]]):.6f})")
+    print(f"{who}: {len(got)} greedy tokens, identical to the oracle's at {len(got) - len(div)}; different at "
+          f"near-ties {[(i, got[i], t['oracle'][i], round(t['margins'][i], 6)) for i in div]}")
+    return div
 
 
 @pytest.mark.parametrize("mk", ["0", "1"])
-def test_1b_256_greedy_steps_identical_to_oracle(llama_1b_full, monkeypatch, mk):
-    """The engine's 256 free-running greedy tokens (after the prompt's own
-    token) equal the oracle's, through the per-op graph (mk=0) and through the
-    persistent decode kernel (mk=1)."""
+def test_1b_256_greedy_steps_vs_oracle(llama_1b_full, monkeypatch, mk):
+    """The engine decodes 256 greedy steps at full 1B depth feeding its own
+    token back on the device, through the per-op graph (mk=0) and the
+    persistent decode kernel (mk=1).  Its tokens equal the oracle's at every
+    step; where the oracle's two best logits tie in fp16 (equal, or within two
+    rounding steps) the two fp32 summation orders may pick different members
+    of the tie, which is reported, and the engine then continues from the
+    oracle's token so that the rest of the sequence is still compared."""
     monkeypatch.setenv("WUKONG_MEGAKERNEL", mk)
     t = llama_1b_full
     L = wk.lib()
@@ -119,26 +135,27 @@ def test_1b_256_greedy_steps_identical_to_oracle(llama_1b_full, monkeypatch, mk)
     pids, ptok = up(t["prompt"]), alloc(4)
     wk.check(L.wk_model_prefill(m, pids, 1, t["prompt"].shape[1], ptok))
     got = [int(down(ptok, 1, np.int32)[0])]
-    for _ in range(STEPS_256):
-        wk.check(L.wk_model_decode_step(m))  # the engine feeds its own token back on the device
+    for s in range(STEPS_256):
+        if got[-1] != t["oracle"][s]:
+            fix = np.array([t["oracle"][s]], np.int32)
+            L.cuda_to_device(L.wk_model_next_ids(m), fix.ctypes.data_as(ctypes.c_void_p), 4)
+        wk.check(L.wk_model_decode_step(m))
         got.append(int(down(L.wk_model_tokens(m), 1, np.int32)[0]))
     launches = L.wk_model_step_launches(m)
     L.wk_model_destroy(m)
     free(pids, ptok)
     assert (launches == 1) == (mk == "1")
-    i = _first_mismatch(got, t["oracle"])
-    print(f"1B 256-step greedy: smallest oracle top-2 margin {min(t['margins']):.6f} at step "
-          f"{int(np.argmin(t['margins']))}; distinct tokens {len(set(got))}")
-    assert i is None, (f"token {i} differs: engine {got[i]}, oracle {t['oracle'][i]}, oracle top-2 margin "
-                       f"{t['margins'][i]:.6f}")
+    div = _check_sequence(got, t, "engine" + (" (persistent kernel)" if mk == "1" else ""))
+    assert set(div) <= set(t["ties"])
 
 
 @pytest.mark.skipif(not os.path.exists(orc.REF_LIB_PATH), reason="oracle/_ref not built")
-def test_1b_256_greedy_steps_identical_to_reference_cuda_cu(llama_1b_full):
-    """The reference's own cuda.cu (built unmodified) runs the reference's Go
-    generate loop (full re-prefill per token, llm/model.go:116-178) through
-    the C++ host mirror; its 256 greedy tokens equal the oracle's and so the
-    engine's (previous test)."""
+def test_1b_256_greedy_steps_reference_cuda_cu_vs_oracle(llama_1b_full):
+    """The reference's own cuda.cu (built unmodified) through the reference's
+    Go call sequence (Predict re-runs the whole sequence each step,
+    llm/llama.go:117-154, llm/model.go:116-178) in the C++ host mirror, on the
+    oracle's token sequence: its 257 predictions equal the oracle's except at
+    the oracle's fp16 near-ties -- the same tolerance as the engine's."""
     t = llama_1b_full
     ref = ctypes.CDLL(orc.REF_LIB_PATH, mode=ctypes.RTLD_LOCAL)
     for name, (res, args) in wk.ABI.items():
@@ -164,20 +181,24 @@ def test_1b_256_greedy_steps_identical_to_reference_cuda_cu(llama_1b_full):
     rm.token_embd, rm.output, rm.output_norm = (rup(t["w"][k]) for k in ("token_embd", "output", "output_norm"))
     h, _ = host_mirror(rm, t["cfg"], wk.Q8_0, wk.Q8_0, wk.F16, t["ctx"], lib_handle=ref._handle)
     L = wk.lib()
-    out = np.zeros(STEPS_256 + 1, np.int32)
-    prompt = np.ascontiguousarray(t["prompt"][0])
-    rc = L.wk_host_llama_generate(h, prompt.ctypes.data_as(ctypes.c_void_p), len(prompt), STEPS_256 + 1,
-                                  out.ctypes.data_as(ctypes.c_void_p))
-    err = L.wk_host_last_error()
+    seq = np.concatenate([t["prompt"][0], np.array(t["oracle"], np.int32)])
+    out = np.zeros(1, np.int32)
+    got, rc, err = [], 0, b""
+    for i in range(STEPS_256 + 1):
+        ids = np.ascontiguousarray(seq[:128 + i].reshape(1, -1))
+        rc = L.wk_host_llama_predict(h, ids.ctypes.data_as(ctypes.c_void_p), 1, ids.shape[1],
+                                     out.ctypes.data_as(ctypes.c_void_p))
+        if rc != 0:
+            err = L.wk_host_last_error()
+            break
+        got.append(int(out[0]))
     L.wk_host_llama_destroy(h)
     for p in ptrs:
         ref.cuda_free(p)
     ref.cuda_fini()
     assert rc == 0, err
-    got = out.tolist()
-    i = _first_mismatch(got, t["oracle"])
-    assert i is None, (f"token {i} differs: reference cuda.cu {got[i]}, oracle {t['oracle'][i]}, oracle top-2 "
-                       f"margin {t['margins'][i]:.6f}")
+    div = _check_sequence(got, t, "reference cuda.cu")
+    assert set(div) <= set(t["ties"])
 
 
 # ------------------------------------------------------------------ head_dim 128 (8B widths)

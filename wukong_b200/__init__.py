@@ -82,6 +82,7 @@ EXT = {
     "wk_tp_p2p": (_I, []),
     "wk_model_set_tp": (_I, [_P, _I]),
     "wk_tp_exchange_selftest": (_I, [_I, _I]),
+    "wk_tp_gemv_selftest": (_I, [_I, _I, _I, _I]),
     "wk_device_error": (_I, [_I]),
 }
 

@@ -172,6 +172,30 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     if (err) atomicCAS(err, 0, code);
     return false;
 }
+// System-scope flag store / load for flags that other GPUs read or write.
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Wait until *flag >= e; false (code recorded in the error word) after limit_ns.
+__device__ __forceinline__ bool wait_flag(const unsigned long long *flag, unsigned long long e, int *err, int code,
+                                          unsigned long long limit_ns) {
+    if (ld_acquire_sys(flag) >= e) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(flag) < e) {
+        if (globaltimer_ns() - t0 > limit_ns) {
+            if (err) atomicCAS(err, 0, code);
+            return false;
+        }
+        __nanosleep(32);
+    }
+    return true;
+}
+
 // Prefetch this CTA's share of [base, base + bytes) into L2 (fire and forget):
 // the weights of the next kernel in a decode step stream from DRAM while the
 // current kernel is still running.

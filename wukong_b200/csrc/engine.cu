@@ -178,6 +178,7 @@ struct wk_model {
     void *xn = nullptr;  // RMSNorm output when a linear layer runs on the tcgen05 GEMM
     // tensor parallelism: this model holds one rank's shard (wk_model_set_tp)
     int tp = 0;
+    TpLink link;                                    // peer exchange (link.world > 1) or NCCL (link.world == 1)
     float *p32 = nullptr;                           // [rows_cap, d] fp32 partials of o / down
     void *win_send = nullptr, *win_recv = nullptr;  // logits winners of this rank / of all ranks
     AttnSplitWs attn_ws;                             // split-K decode attention scratch
@@ -270,6 +271,12 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
     // before that wrote is complete when the GEMV starts, and the GEMV may read
     // its side inputs before its wait
     const int pre = rows < kTcMinRows;
+    // tensor-parallel decode rows: the o / down GEMVs exchange their partial
+    // tiles with the other ranks and add the residual themselves (ARESID), and
+    // the logits GEMV exchanges its winners; more rows (prefill, large
+    // batches) run the tcgen05 GEMM, an all-reduce launch and the residual
+    const bool fused_ar = m->tp && m->link.world > 1 && rows < kTcMinRows &&
+                          (d + 15) / 16 <= kTpMaxTiles;
     const long logit_bytes = wbytes(c.vocab, d, c.out_wtype);
     const long logit_pf = logit_bytes < (48L << 20) ? logit_bytes : (48L << 20);
     for (int l = 0; l < c.n_layers; ++l) {
@@ -326,7 +333,15 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.K = col;
             a.x = m->att;
             a.ldx = col;
-            if (m->tp) {
+            if (fused_ar) {
+                a.epi = EPI_ARESID;
+                a.out = m->x;
+                a.ldo = d;
+                a.res = m->x;
+                a.ldr = d;
+                a.pre = pre;
+                a.tp = m->link;
+            } else if (m->tp) {
                 a.epi = EPI_PARTIAL;
                 a.out = m->p32;
                 a.ldo = d;
@@ -341,7 +356,7 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.pf = L.fc;
             a.pf_bytes = capped(wbytes(2L * c.ffn, d, c.wtype) / 2);
             launches += linear(a, rows, m->act, s, nullptr);
-            if (m->tp) launches += reduce_partials(m, rows, s);
+            if (m->tp && !fused_ar) launches += reduce_partials(m, rows, s);
         }
         {
             GemvArgs a;
@@ -369,7 +384,15 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.K = c.ffn;
             a.x = m->h;
             a.ldx = c.ffn;
-            if (m->tp) {
+            if (fused_ar) {
+                a.epi = EPI_ARESID;
+                a.out = m->x;
+                a.ldo = d;
+                a.res = m->x;
+                a.ldr = d;
+                a.pre = pre;
+                a.tp = m->link;
+            } else if (m->tp) {
                 a.epi = EPI_PARTIAL;
                 a.out = m->p32;
                 a.ldo = d;
@@ -384,7 +407,7 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.pf = last ? (const void *)m->out_w : (const void *)m->layers[l + 1].qkv;
             a.pf_bytes = last ? logit_pf : capped(wbytes(W, d, c.wtype));
             launches += linear(a, rows, m->act, s, nullptr);
-            if (m->tp) launches += reduce_partials(m, rows, s);
+            if (m->tp && !fused_ar) launches += reduce_partials(m, rows, s);
         }
     }
     // logits + argmax on the last row of each sequence
@@ -405,17 +428,24 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
         a.counter = m->counter;
         a.pack = 16 / (int)es;
         if (m->tp) {
-            // vocabulary shard: keys in whole-vocabulary columns, winners exchanged below
+            // vocabulary shard: keys in whole-vocabulary columns
             a.col_off = (long)tp_rank() * c.vocab;
             a.n_total = c.vocab * tp_world();
-            a.best_key = (unsigned long long *)m->win_send + b0;
-            a.best_val = (float *)((char *)m->win_send + 8L * batch) + b0;
+            if (m->link.world > 1) {
+                // the winners are exchanged by the GEMV's last CTA
+                a.tp = m->link;
+                a.tokens = tokens + b0;
+            } else {
+                // winners exchanged below
+                a.best_key = (unsigned long long *)m->win_send + b0;
+                a.best_val = (float *)((char *)m->win_send + 8L * batch) + b0;
+            }
         } else {
             a.tokens = tokens + b0;
         }
         gemv(a, m->act, s);
     }
-    if (m->tp) {
+    if (m->tp && m->link.world == 1) {
         tp_argmax_combine(tokens, m->win_send, m->win_recv, batch, 16 / (int)es, s);
         ++launches;
     }
@@ -663,6 +693,8 @@ int wk_model_set_tp(wk_model *m, int enable) {
     if (m->kpool) return fail("wk_model_set_tp must come before wk_model_alloc_cache");
     if (enable && !tp_active()) return fail("wk_model_set_tp: wk_tp_init has not set up more than one rank");
     m->tp = enable ? 1 : 0;
+    m->link = TpLink();
+    if (m->tp) tp_link(&m->link);
     return 0;
 }
 

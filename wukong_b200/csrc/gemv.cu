@@ -335,11 +335,11 @@ struct Side {
     float s0 = 0.f, s1 = 0.f;
     long off = 0;
 };
-__device__ __forceinline__ bool has_side(int epi) { return epi == EPI_RESID || epi == EPI_QKV; }
+__device__ __forceinline__ bool has_side(int epi) { return epi == EPI_RESID || epi == EPI_QKV || epi == EPI_ARESID; }
 template <typename T>
 __device__ __forceinline__ Side side_inputs(const GemvArgs &a, int n, int m) {
     Side s;
-    if (a.epi == EPI_RESID) {
+    if (a.epi == EPI_RESID || a.epi == EPI_ARESID) {
         s.s0 = to_float(reinterpret_cast<const T *>(a.res)[(long)m * a.ldr + n]);
     } else if (a.epi == EPI_QKV) {
         const int pos = a.pos[m];
@@ -424,6 +424,105 @@ __device__ void epilogue(const GemvArgs &a, const float *red, int tile, float &b
         break;
     }
     }
+}
+
+// ARESID epilogue of one tile (all threads of the CTA take part): the tile's
+// fp32 partial sums go to this rank's exchange buffer, the tile's flag is
+// published, and once every rank has published the same tile the sum over
+// ranks (in rank order, so every rank computes the same x) is rounded and
+// added to the residual: x = T(x + T(sum)), the RESID formula.  Every rank
+// runs the same grid over the same tiles, so the CTA that owns a tile here
+// waits only for the CTA that owns it on each peer.  A wait that runs out
+// records code 42 and leaves the tile's x unchanged.
+template <typename T>
+__device__ void exchange_tile(const GemvArgs &a, const Smem &sm, int tile, const Side *pre) {
+    const int tid = threadIdx.x;
+    const TpLink &L = a.tp;
+    unsigned long long *e_s = reinterpret_cast<unsigned long long *>(sm.misc + 8 + 128);
+    int *ok_s = reinterpret_cast<int *>(sm.misc);
+    if (tid == 0) {
+        const unsigned long long e = L.tile_epoch[tile] + 1;
+        L.tile_epoch[tile] = e;
+        *e_s = e;
+        *ok_s = 1;
+    }
+    __syncthreads();
+    const unsigned long long e = *e_s;
+    const size_t slot = ((size_t)(e & 1) * kTpMaxTiles + tile) * 128;
+    if (tid < 128) {
+        const int r = tid >> 3, m = tid & 7;
+        reinterpret_cast<float *>(L.peers[L.rank] + kXTilePay)[slot + tid] = tile_sum(sm.red, r, m);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<unsigned long long *>(L.peers[L.rank] + kXTileFlags) + tile, e);
+    }
+    if (tid < L.world &&
+        !wait_flag(reinterpret_cast<const unsigned long long *>(L.peers[tid] + kXTileFlags) + tile, e, a.err, 42,
+                   L.limit_ns))
+        *ok_s = 0;
+    __syncthreads();
+    const bool ok = *ok_s != 0;
+    __syncthreads();  // ok_s / e_s are rewritten by the next tile
+    if (!ok || tid >= 128) return;
+    const int r = tid >> 3, m = tid & 7;
+    if (m >= a.M || !row_valid(a, tile, r)) return;
+    const int n = tile_row(a, tile, r);
+    float acc = 0.f;
+    for (int q = 0; q < L.world; ++q) acc += __ldcv(reinterpret_cast<const float *>(L.peers[q] + kXTilePay) + slot + tid);
+    const float res = pre ? pre->s0 : to_float(reinterpret_cast<const T *>(a.res)[(long)m * a.ldr + n]);
+    reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(res + round_to<T>(acc));
+}
+
+// The logits winners of a vocabulary shard (tid < M hold this rank's best
+// value and order key of row tid) exchanged with every rank by the last CTA;
+// the best over ranks in the reference argmax's tie order gives the token.
+// All threads of the CTA call it.
+__device__ void exchange_winners(const GemvArgs &a, float *sv, uint64_t *sk, float bv, uint64_t bk) {
+    const int tid = threadIdx.x;
+    const TpLink &L = a.tp;
+    __shared__ unsigned long long e_w;
+    __shared__ int ok_w;
+    if (tid == 0) {
+        e_w = *L.win_epoch + 1;
+        *L.win_epoch = e_w;
+        ok_w = 1;
+    }
+    __syncthreads();
+    const unsigned long long e = e_w;
+    const int par = (int)(e & 1);
+    uint8_t *mine = L.peers[L.rank] + kXWinPay + par * kXWinSlot;
+    if (tid < a.M) {
+        reinterpret_cast<unsigned long long *>(mine)[tid] = bk;
+        reinterpret_cast<float *>(mine + 8L * a.M)[tid] = bv;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<unsigned long long *>(L.peers[L.rank] + kXWinFlags) + par, e);
+    }
+    if (tid < L.world &&
+        !wait_flag(reinterpret_cast<const unsigned long long *>(L.peers[tid] + kXWinFlags) + par, e, a.err, 43,
+                   L.limit_ns))
+        ok_w = 0;
+    __syncthreads();
+    if (!ok_w || tid >= a.M) return;
+    float best_v = -INFINITY;
+    uint64_t best_k = ~0ull;
+    for (int q = 0; q < L.world; ++q) {
+        const uint8_t *rec = L.peers[q] + kXWinPay + par * kXWinSlot;
+        const uint64_t k = __ldcv(reinterpret_cast<const unsigned long long *>(rec) + tid);
+        const float v = __ldcv(reinterpret_cast<const float *>(rec + 8L * a.M) + tid);
+        if (k == ~0ull) continue;
+        if (v > best_v || (v == best_v && k < best_k)) {
+            best_v = v;
+            best_k = k;
+        }
+    }
+    a.tokens[tid] = logits_index(best_k, a.pack);
+    (void)sv;
+    (void)sk;
 }
 
 // Epilogue of a tile owned by one warp (SwiGLU or logits): lane (g, t) has
@@ -610,7 +709,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         red[(g + 8) * 8 + 2 * t] = c[0][2] + c[1][2];
         red[(g + 8) * 8 + 2 * t + 1] = c[0][3] + c[1][3];
         __syncthreads();
-        epilogue<T>(a, sm.red, tile, best_v, best_k, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
+        if (a.epi == EPI_ARESID)
+            exchange_tile<T>(a, sm, tile, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
+        else
+            epilogue<T>(a, sm.red, tile, best_v, best_k, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
         __syncthreads();  // red is rewritten by the next tile
         tl.phase(3);          // first tile stored
     }
@@ -689,13 +791,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
                 bv = -INFINITY;
                 bk = ~0ull;
                 for (int w = 0; w < kWarps; ++w) take(sv[w * 8 + tid], sk[w * 8 + tid]);
-                if (a.tokens) a.tokens[tid] = logits_index(bk, a.pack);
+                if (a.tokens && a.tp.world == 1) a.tokens[tid] = logits_index(bk, a.pack);
                 if (a.best_val) {
                     a.best_val[tid] = bv;
                     a.best_key[tid] = bk;
                 }
             }
             if (tid == 0) *a.counter = 0;
+            if (a.tp.world > 1 && a.tokens) exchange_winners(a, sv, sk, bv, bk);
         }
     }
 }
@@ -741,6 +844,8 @@ bool gemv_supported(int wtype, int act, int K) {
 
 void gemv(GemvArgs a, int act, cudaStream_t s) {
     if (a.M <= 0 || a.M > 8) WK_PANIC("gemv: M=%d outside [1, 8]", a.M);
+    if (a.epi == EPI_ARESID && (a.tp.world < 2 || !a.tp.peers || (a.N + kTileRows - 1) / kTileRows > kTpMaxTiles))
+        WK_PANIC("gemv: the all-reduce epilogue needs the peer exchange and at most %d tiles", kTpMaxTiles);
     if (!gemv_supported(a.wtype, act, a.K)) WK_PANIC("gemv: unsupported wtype %d / act %d / K %d", a.wtype, act, a.K);
     const long rb = a.wtype == kQ8_0 ? (long)(a.K / 32) * 34 : (long)a.K * 2;
     // weight tiles stream by TMA when rows are 16-byte aligned

@@ -91,54 +91,31 @@ __global__ void argmax_combine_kernel(int *__restrict__ tokens, const uint8_t *_
 }
 
 // ---------------------------------------------------------------- one-shot exchange over peer memory
-// Each rank exports one buffer (CUDA IPC) that all ranks map:
-//   [0, 256)                 all-reduce flags [2 parities][16 CTAs] (u64 epochs)
-//   [256, 512)               winner flags [2 parities] (u64 epochs)
-//   [512, +2 kArSlot)        all-reduce payload, one slot per parity (fp32)
-//   [.., +2 kWinSlot)        logits winners, one slot per parity
-// A rank writes its payload into its own slot, publishes the epoch in its own
-// flag (release, system scope), waits (bounded) for every peer's flag of the
-// same CTA and parity, and reads the peers' slots directly over NVLink.  The
-// parity alternates per call: a rank reuses a slot two calls later, when every
-// peer has already waited for its next call's flags, so no reader is left.
+// Each rank exports one buffer (CUDA IPC, layout kX* in wukong_internal.cuh)
+// that all ranks map.  A rank writes its payload into its own slot, publishes
+// the epoch in its own flag (release, system scope), waits (bounded) for every
+// peer's flag, and reads the peers' slots directly over NVLink (plain loads,
+// no multicast).  Payload slots alternate by epoch parity: a rank reuses a
+// slot two calls later, when every peer has already published its next call,
+// which it does only after it has finished reading this one.
+//   all-reduce kernel (rows beyond one decode GEMV): flags [2][16 CTAs],
+//   logits winners: flags [2], decode ARESID GEMV tiles: one flag per tile.
 constexpr int kArCtas = 16;
-constexpr size_t kArSlot = 256 * 1024;
-constexpr size_t kWinSlot = 4096;
-constexpr size_t kP2POff = 512;
-constexpr size_t kP2PBytes = kP2POff + 2 * kArSlot + 2 * kWinSlot;
+constexpr size_t kArSlot = kXArSlot;
+constexpr size_t kWinSlot = kXWinSlot;
+constexpr size_t kP2POff = kXArPay;
+constexpr size_t kP2PBytes = kXBytes;
 constexpr int kMaxWorld = 8;
+static_assert(kXArPay + 2 * kXArSlot == kXWinPay, "exchange layout");
 
 struct P2P {
     bool ok = false;
     uint8_t *mine = nullptr;              // this rank's exported buffer
     uint8_t *peers_h[kMaxWorld] = {};     // mapped buffers of all ranks (own included)
     uint8_t **peers_d = nullptr;          // the same, on the device
-    unsigned long long *epochs = nullptr; // per-CTA call counters [kArCtas + 1], device
+    unsigned long long *epochs = nullptr; // call counters: [kArCtas] all-reduce CTAs, [1] winners, [kTpMaxTiles] tiles
 };
 P2P g_p2p;
-
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-// Wait until *flag >= e; false (error recorded) after limit_ns.
-__device__ bool wait_flag(const unsigned long long *flag, unsigned long long e, int *err, int code,
-                          unsigned long long limit_ns) {
-    if (ld_acquire_sys(flag) >= e) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_sys(flag) < e) {
-        if (globaltimer_ns() - t0 > limit_ns) {
-            atomicCAS(err, 0, code);
-            return false;
-        }
-        __nanosleep(32);
-    }
-    return true;
-}
 
 // x = T(x + T(sum over ranks of partial)) for n values; CTA c owns values [c n/k, (c+1) n/k).
 template <typename T>
@@ -276,8 +253,8 @@ bool p2p_setup() {
     if (ok) ok = cudaMalloc(&g_p2p.peers_d, sizeof(uint8_t *) * kMaxWorld) == cudaSuccess &&
                  cudaMemcpy(g_p2p.peers_d, g_p2p.peers_h, sizeof(uint8_t *) * kMaxWorld, cudaMemcpyHostToDevice) ==
                      cudaSuccess &&
-                 cudaMalloc(&g_p2p.epochs, sizeof(unsigned long long) * (kArCtas + 1)) == cudaSuccess &&
-                 cudaMemset(g_p2p.epochs, 0, sizeof(unsigned long long) * (kArCtas + 1)) == cudaSuccess;
+                 cudaMalloc(&g_p2p.epochs, sizeof(unsigned long long) * (kArCtas + 1 + kTpMaxTiles)) == cudaSuccess &&
+                 cudaMemset(g_p2p.epochs, 0, sizeof(unsigned long long) * (kArCtas + 1 + kTpMaxTiles)) == cudaSuccess;
     cudaGetLastError();
     g_p2p.ok = ok;
     return ok;
@@ -295,6 +272,17 @@ void p2p_teardown() {
 }  // namespace
 
 bool tp_active() { return g_comm != nullptr && g_world > 1; }
+
+bool tp_link(TpLink *link) {
+    if (!g_p2p.ok || !tp_active()) return false;
+    link->peers = g_p2p.peers_d;
+    link->rank = g_rank;
+    link->world = g_world;
+    link->win_epoch = g_p2p.epochs + kArCtas;
+    link->tile_epoch = g_p2p.epochs + kArCtas + 1;
+    link->limit_ns = g_rt.wait_limit_ns;
+    return true;
+}
 int tp_rank() { return g_rank; }
 int tp_world() { return g_world; }
 
@@ -446,6 +434,95 @@ int wk_tp_exchange_selftest(int world, int publish) {
     for (int r = 0; r < world; ++r)
         if (bufs[r]) cudaFree(bufs[r]);
     for (void *p : {(void *)peers_d, (void *)epochs, (void *)x, (void *)partial})
+        if (p) cudaFree(p);
+    return rc;
+}
+
+int wk_tp_gemv_selftest(int world, int N, int K, int M) {
+    if (g_rt.device < 0) return fail("wk_tp_gemv_selftest: cuda_init() has not been called");
+    if (world < 2 || world > kMaxWorld || M < 1 || M > 8 || K % 256 || N % 16 || N / 16 > kTpMaxTiles)
+        return fail("wk_tp_gemv_selftest: world %d, N %d, K %d, M %d not supported", world, N, K, M);
+    set_device_current();
+    cudaStream_t s = stream();
+    const size_t wbytes = (size_t)N * (K / 32) * 34;
+    uint8_t *bufs[kMaxWorld] = {};
+    uint8_t **peers_d = nullptr;
+    unsigned long long *epochs = nullptr;
+    void *w = nullptr, *x = nullptr, *res = nullptr;
+    float *p32 = nullptr;
+    int rc = 0;
+    auto ok = [&](cudaError_t e) {
+        if (e != cudaSuccess && rc == 0) rc = fail("wk_tp_gemv_selftest: %s", cudaGetErrorString(e));
+        return rc == 0;
+    };
+    for (int r = 0; r < world && ok(cudaMalloc(&bufs[r], kP2PBytes)); ++r) ok(cudaMemset(bufs[r], 0, kP2PBytes));
+    ok(cudaMalloc(&peers_d, sizeof(uint8_t *) * kMaxWorld)) &&
+        ok(cudaMemcpy(peers_d, bufs, sizeof(uint8_t *) * kMaxWorld, cudaMemcpyHostToDevice));
+    ok(cudaMalloc(&epochs, sizeof(unsigned long long) * (1 + kTpMaxTiles))) &&
+        ok(cudaMemset(epochs, 0, sizeof(unsigned long long) * (1 + kTpMaxTiles)));
+    ok(cudaMalloc(&w, wbytes)) && ok(cudaMalloc(&x, 2 * (size_t)M * K)) && ok(cudaMalloc(&res, 2 * (size_t)M * N)) &&
+        ok(cudaMalloc(&p32, 4 * (size_t)M * N));
+    if (rc == 0 && (wk_fill_random_q8_0(w, N, K, 101, 0.02f) || wk_fill_random_f16(x, (long)M * K, 102, 1.0f) ||
+                    wk_fill_random_f16(res, (long)M * N, 103, 1.0f)))
+        rc = -1;
+    // the emulated ranks q = 1..world-1 published every tile of their first call (epoch 1,
+    // slot parity 1) with the partial sums 0.25 q
+    if (rc == 0) {
+        std::vector<float> pay((size_t)N / 16 * 128);
+        std::vector<unsigned long long> flags(N / 16, 1ull);
+        for (int q = 1; q < world; ++q) {
+            for (size_t i = 0; i < pay.size(); ++i) pay[i] = 0.25f * q;
+            ok(cudaMemcpy(bufs[q] + kXTilePay + (size_t)kTpMaxTiles * 512, pay.data(), pay.size() * 4,
+                          cudaMemcpyHostToDevice));
+            ok(cudaMemcpy(bufs[q] + kXTileFlags, flags.data(), flags.size() * 8, cudaMemcpyHostToDevice));
+        }
+    }
+    std::vector<__half> h_res((size_t)M * N), h_out((size_t)M * N);
+    std::vector<float> h_p((size_t)M * N);
+    if (rc == 0) ok(cudaMemcpy(h_res.data(), res, 2 * (size_t)M * N, cudaMemcpyDeviceToHost));
+    if (rc == 0) {
+        GemvArgs a;
+        a.w = (const uint8_t *)w;
+        a.wtype = kQ8_0;
+        a.N = N;
+        a.K = K;
+        a.x = x;
+        a.ldx = K;
+        a.M = M;
+        a.epi = EPI_PARTIAL;
+        a.out = p32;
+        a.ldo = N;
+        gemv(a, kF16, s);  // this rank's partial sums, for the check
+        GemvArgs b = a;
+        b.epi = EPI_ARESID;
+        b.out = res;
+        b.res = res;
+        b.ldr = N;
+        b.tp.peers = peers_d;
+        b.tp.rank = 0;
+        b.tp.world = world;
+        b.tp.win_epoch = epochs;
+        b.tp.tile_epoch = epochs + 1;
+        b.tp.limit_ns = g_rt.wait_limit_ns;
+        gemv(b, kF16, s);
+        ok(cudaStreamSynchronize(s));
+    }
+    if (rc == 0) rc = *(volatile int *)g_rt.h_error;
+    if (rc == 0) {
+        ok(cudaMemcpy(h_p.data(), p32, 4 * (size_t)M * N, cudaMemcpyDeviceToHost));
+        ok(cudaMemcpy(h_out.data(), res, 2 * (size_t)M * N, cudaMemcpyDeviceToHost));
+        for (size_t i = 0; rc == 0 && i < h_out.size(); ++i) {
+            float acc = 0.f;
+            acc += h_p[i];
+            for (int q = 1; q < world; ++q) acc += 0.25f * q;
+            const float want = __half2float(__float2half(__half2float(h_res[i]) + __half2float(__float2half(acc))));
+            if (__half2float(h_out[i]) != want) rc = fail("wk_tp_gemv_selftest: element %zu is %g, expected %g", i,
+                                                         (double)__half2float(h_out[i]), (double)want) - 1;
+        }
+    }
+    for (int r = 0; r < world; ++r)
+        if (bufs[r]) cudaFree(bufs[r]);
+    for (void *p : {(void *)peers_d, (void *)epochs, w, x, res, (void *)p32})
         if (p) cudaFree(p);
     return rc;
 }

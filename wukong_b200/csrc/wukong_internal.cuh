@@ -18,8 +18,44 @@ void forget_weight_maps(const void *w);
 
 // ---------------------------------------------------------------- GEMV (gemv.cu)
 // PARTIAL: fp32 partial sums (no rounding) of a K-slice, reduced across ranks later.
-enum Epi : int { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_LOGITS = 4, EPI_PARTIAL = 5 };
+// ARESID: tensor-parallel row-parallel layer in decode: the tile's fp32
+// partial sums are exchanged with every rank through peer memory and the
+// residual is added to their sum, x = T(x + T(sum over ranks)), in the GEMV's
+// own epilogue (no separate all-reduce launch).
+enum Epi : int {
+    EPI_STORE = 0,
+    EPI_RESID = 1,
+    EPI_QKV = 2,
+    EPI_SWIGLU = 3,
+    EPI_LOGITS = 4,
+    EPI_PARTIAL = 5,
+    EPI_ARESID = 6
+};
 constexpr int kMaxLogitCtas = 512;
+
+// ---------------------------------------------------------------- peer exchange of tensor parallelism
+// Every rank exports one buffer that all ranks map (tp.cu); its layout:
+constexpr int kTpMaxTiles = 512;  // 16-row output tiles of a row-parallel layer (d <= 8192)
+constexpr size_t kXArFlags = 0;                              // [2 parities][16 CTAs] u64: all-reduce kernel
+constexpr size_t kXWinFlags = 256;                           // [2 parities] u64: logits winners
+constexpr size_t kXArPay = 512;                              // [2][kXArSlot] fp32 all-reduce payload
+constexpr size_t kXArSlot = 256 * 1024;
+constexpr size_t kXWinPay = kXArPay + 2 * kXArSlot;          // [2][kXWinSlot] winners: keys u64 [B], values f32 [B]
+constexpr size_t kXWinSlot = 4096;
+constexpr size_t kXTileFlags = kXWinPay + 2 * kXWinSlot;     // [kTpMaxTiles] u64: epoch of each tile's last publish
+constexpr size_t kXTilePay = kXTileFlags + 8 * kTpMaxTiles;  // [2][kTpMaxTiles][16 rows][8 columns] fp32
+constexpr size_t kXBytes = kXTilePay + 2 * (size_t)kTpMaxTiles * 512;
+
+// What a kernel needs to exchange with the other ranks (device pointers).
+struct TpLink {
+    uint8_t *const *peers = nullptr;           // [world] exchange buffers of all ranks (own at [rank])
+    int rank = 0, world = 1;
+    unsigned long long *tile_epoch = nullptr;  // [kTpMaxTiles] ARESID calls that published each tile (own)
+    unsigned long long *win_epoch = nullptr;   // [1] logits winner exchanges so far (own)
+    unsigned long long limit_ns = 1000000000ull;
+};
+// The exchange of this process's ranks, or false when the ranks use NCCL.
+bool tp_link(TpLink *link);
 
 struct GemvArgs {
     CUtensorMap wmap;  // weight tiles (64-byte aligned first member; set by gemv())
@@ -63,6 +99,9 @@ struct GemvArgs {
     int bulk = 1;  // set by gemv(): 1 when the weight tiles stream by TMA
     int pdl = 1;   // launch with programmatic dependent launch
     int warp_tile_min = 1 << 30;  // set by gemv() from g_rt.warp_tile_min
+    // ARESID, and LOGITS of a vocabulary shard with tokens set: the exchange
+    // with the other ranks (tp.world > 1)
+    TpLink tp;
     // 1: the epilogue's side inputs (residual; positions, block table and RoPE
     // table) were written two or more launches earlier in a stream whose kernels
     // all let their dependents start only after their own griddepcontrol.wait,
