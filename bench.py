@@ -341,6 +341,70 @@ def run_op(spec, copies=8, reps=20):
     L.cuda_fini()
 
 
+def prefill_flops(cfg, B, T):
+    """Dense FLOPs of one prefill: every linear layer on all B T rows, causal
+    attention (q.k and p.v over the keys at or before each row), logits of the
+    last row of each sequence."""
+    d, H, Hk, D, F, V, L = (cfg[k] for k in ("d", "H", "Hk", "D", "F", "V", "L"))
+    linear = L * ((H + 2 * Hk) * D * d + d * H * D + 2 * F * d + d * F)
+    attn = L * H * D * 2 * 2 * (T * (T + 1) // 2)
+    return 2.0 * linear * B * T + attn * B + 2.0 * V * d * B
+
+
+def run_prefill(args):
+    """Prefill throughput: wk_model_prefill of B prompts of T tokens (the
+    tcgen05 GEMMs with fused dequantisation and epilogues, the flash-style
+    prefill attention, the logits of the last rows), inputs resident in HBM;
+    tokens/s and the fraction of the measured sustained bf16 tensor peak."""
+    import torch
+    import wukong_b200 as wk
+    from wukong_b200.engine import LLAMA, Engine, SyntheticLlama
+    L = wk.lib()
+    L.cuda_init(0)
+    stream = torch.cuda.ExternalStream(L.wk_stream())
+    cfg = dict(LLAMA[args.model])
+    wt = wk.F16 if args.wtype == "f16" else wk.Q8_0
+    B, T = args.batch, args.prompt
+    sm = SyntheticLlama(cfg, T + 8, wtype=wt, out_type=wt, seed=SEED)
+    eng = Engine.from_synthetic(sm, max_batch=B)
+    prompt = np.random.default_rng(7).integers(0, cfg["V"], size=(B, T)).astype(np.int32)
+    d_prompt = L.cuda_malloc(prompt.nbytes)
+    L.cuda_to_device(d_prompt, prompt.ctypes.data_as(ctypes.c_void_p), prompt.nbytes)
+    for _ in range(args.warmup):
+        eng.prefill(d_prompt, B, T)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    with Clocks(0) as clk:
+        for _ in range(args.steps):
+            torch.cuda.synchronize()
+            e0.record(stream)
+            eng.prefill(d_prompt, B, T)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    flops = prefill_flops(cfg, B, T)
+    pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {"bf16_tflops_sustained": 1400.0}
+    tf = flops / (ms / 1e3) / 1e12
+    line = {"metric": "prefill tokens/sec", "value": B * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "dtype": "f16 x f16 -> f32" if wt == wk.F16 else "int8 x f16 -> f32", "data": "synthetic",
+            "config": {"workload": f"{NAMES[args.model]} {args.wtype.upper()} prefill, batch {B}, {T}-token prompt",
+                       "model": NAMES[args.model], "batch": B, "prompt": T,
+                       "timing": "median of single prefills (CUDA events), weights read per prefill exceed L2"},
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                         "frac": tf / pk["bf16_tflops_sustained"], "flops_per_step": flops,
+                         "peak_source": "measured sustained bf16 (cuBLAS) of MEASURED_PEAKS.json"},
+            "gpu_launches": None, "clocks": clk.summary()}
+    print(json.dumps(line))
+    eng.destroy()
+    sm.free()
+    L.cuda_free(d_prompt)
+    L.cuda_fini()
+
+
 # ------------------------------------------------------------------ CPU baseline
 def run_cpu(model, B, P, steps, budget_s=25.0):
     """The oracle port (C++ restatement of the reference semantics) on the host
@@ -387,6 +451,9 @@ def main():
                     help="blocks are added until about this much decode time is timed")
     ap.add_argument("--prompt", type=int, default=None, help="prompt tokens (default 128 / 2048 / 4096)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="decode", choices=["decode", "prefill"],
+                    help="prefill: time wk_model_prefill of --batch prompts of --prompt tokens (one JSON line)")
+    ap.add_argument("--wtype", default="q8_0", choices=["q8_0", "f16"], help="linear / output weights (--mode prefill)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--op", default=None, metavar="NxKxM[,...]",
@@ -422,6 +489,9 @@ def main():
 
     if args.op:
         run_op(args.op)
+        return
+    if args.mode == "prefill":
+        run_prefill(args)
         return
 
     if args.impl == "reference":

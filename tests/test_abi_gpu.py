@@ -352,6 +352,36 @@ def test_layers_vs_oracle(dev, wtype, B, Tn):
     free(pf, px, *p.values())
 
 
+@pytest.mark.parametrize("d,H,Hk,D,B,Tn,wtype", [(2048, 32, 8, 64, 1, 512, Q8_0), (2048, 32, 8, 64, 2, 300, F16),
+                                                   (4096, 32, 8, 128, 1, 2048, Q8_0), (1024, 8, 8, 128, 1, 130, BF16),
+                                                   (1024, 16, 2, 64, 1, 200, Q8_0)])
+def test_prefill_attention_sublayer_vs_oracle(dev, d, H, Hk, D, B, Tn, wtype):
+    """The attention sublayer over a long prompt (the flash-style prefill
+    kernel): Llama-3.2-1B widths at 512 and 300 tokens, Llama-3.1-8B widths
+    (head_dim 128) at 2048, and 1 and 8 query heads per KV head."""
+    act = BF16 if wtype == BF16 else F16
+    W = (H + 2 * Hk) * D
+    lw = dict(attn_norm=np.ones(d, np.float32), qkv=_weights(wtype, W, d, 90), o=_weights(wtype, d, H * D, 91))
+    freqs = orc.make_freqs(D, Tn, 500000.0)
+    xd, xf = _acts(act, B * Tn, d, seed=92, std=1.0)
+    p = {k: up(v) for k, v in lw.items()}
+    pf, px = up(freqs), up(xd)
+    dev.cuda_group_query_attention(px, px, pf, p["attn_norm"], p["qkv"], p["o"], B, Tn, H, Hk, D, 1e-5, wtype)
+    x_attn = _from_dev(down(px, (B * Tn, d), np.uint16 if act == BF16 else np.float16), act)
+    xo = xf.reshape(B, Tn, d).copy()
+    kc = np.zeros((B, Hk, Tn, D), np.float32)
+    vc = np.zeros_like(kc)
+    L, pp = orc.lib(), orc._p
+    L.orc_gqa_layer(pp(xo), pp(freqs), pp(lw["attn_norm"]), pp(lw["qkv"]), pp(lw["o"]), B, Tn, 0, H, Hk, D, 1e-5,
+                    wtype, act, pp(kc), pp(vc), Tn)
+    upd, ref = x_attn - xf, xo.reshape(B * Tn, d) - xf
+    nw = float(np.linalg.norm(upd - ref) / np.linalg.norm(ref))
+    print(f"prefill attention {B}x{Tn} d {d} H {H}/{Hk} D {D}: normwise rel-err of the update {nw:.2e}")
+    assert rel_err(upd, ref) <= 2 * tol(act)
+    assert nw <= tol(act)
+    free(pf, px, *p.values())
+
+
 @pytest.mark.parametrize("wtype", [Q8_0, F16])
 def test_classify_predict_vocab_vs_oracle(dev, wtype):
     """Logits over the 128256 vocabulary and the fused argmax (reference tie order)."""

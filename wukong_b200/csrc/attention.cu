@@ -892,6 +892,267 @@ void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq
                                 g_rt.d_error, pf, pf_bytes, early ? 1 : 0));
 }
 
+// ---------------------------------------------------------------- prefill (flash-style, tensor cores)
+// Prefill rows: n consecutive query positions P..P+n-1 of each sequence over
+// its paged K/V (64-token pages = 64-key blocks).  One CTA of 8 warps takes a
+// tile of 128 "query rows" = 128 / G positions x the G query heads of one KV
+// head (position-major), so every K/V block it loads serves all 128 rows; each
+// warp owns 16 rows and keeps Q, the scores and O in mma.sync fragments.
+// Two passes over the key blocks keep the reference's rounding points exactly
+// (cuda.cu:767-852 with :673-765):
+//   pass 1: s_j = T(q . k_j), the row max M of s_j * scale (exact) and the
+//           softmax sum of exp(s_j * scale - M), accumulated per block with
+//           the running-max rescaling (the same sum up to fp32 rounding order);
+//   pass 2: s_j again (same products, same rounding), P_j =
+//           T(T(exp(s_j * scale - M)) * (1 / sum)), O += P . V in fp32, and
+//           finally T(O).
+// K/V blocks stream through a 2-stage shared-memory ring by 16-byte cp.async
+// copies into an XOR-swizzled layout (conflict-free ldmatrix); blocks wholly
+// above a warp's positions are skipped (causal).
+constexpr int kPfRows = 128;  // query rows per CTA (8 warps x 16)
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// byte offset of 16-byte chunk c of row r in a [rows][D] 16-bit tile (D >= 64)
+template <int D> __device__ __forceinline__ uint32_t swz(int r, int c) {
+    return (uint32_t)(r * (D * 2) + ((c ^ (r & 7)) << 4));
+}
+template <typename T> __device__ __forceinline__ uint32_t pack_t2(float a, float b) {
+    T ha = from_float<T>(a), hb = from_float<T>(b);
+    return (uint32_t)*reinterpret_cast<uint16_t *>(&ha) | ((uint32_t)*reinterpret_cast<uint16_t *>(&hb) << 16);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256, D == 64 ? 2 : 1)
+    attn_prefill_kernel(T *__restrict__ out, long out_rs, const T *__restrict__ q, long q_rs, int n, int P, KVPaged kv,
+                        int G, float scale) {
+    constexpr int kCh = D / 8;                 // 16-byte chunks per row
+    constexpr int kTile = kAttnPage * D * 2;   // bytes of one 64-key block
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *Qs = smem;                        // [128][D]
+    uint8_t *Ks = Qs + kPfRows * D * 2;        // [2][64][D]
+    uint8_t *Vs = Ks + 2 * kTile;              // [2][64][D]
+    const int QP = kPfRows / G;
+    const int tile = gridDim.x - 1 - blockIdx.x;  // the longest tiles first
+    const int kvh = blockIdx.y, b = blockIdx.z;
+    const int i0 = tile * QP;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int nkeys = P + min(n, i0 + QP);     // keys 0 .. the tile's last position
+    const int nb = (nkeys + kAttnPage - 1) / kAttnPage;
+    const T *K = reinterpret_cast<const T *>(kv.k);
+    const T *V = reinterpret_cast<const T *>(kv.v);
+    const int *bt = kv.block_table + (long)b * kv.max_pages;
+    // q, K and V of these positions are written by the previous kernel
+    pdl_wait();
+    pdl_trigger();
+
+    // positions of this thread's two rows (g, g + 8 of the warp's 16)
+    const int r0 = warp * 16 + g, r1 = r0 + 8;
+    const int pos0 = P + i0 + r0 / G, pos1 = P + i0 + r1 / G;
+    const int wpos_max = P + i0 + (warp * 16 + 15) / G;  // the warp's last position
+
+    // Q tile (rows past the sequence are zero)
+    for (int idx = tid; idx < kPfRows * kCh; idx += 256) {
+        const int r = idx / kCh, c = idx % kCh;
+        const int i = i0 + r / G;
+        const T *src = q + ((long)b * n + (i < n ? i : 0)) * q_rs + (long)(kvh * G + r % G) * D + c * 8;
+        cp_async16(Qs + swz<D>(r, c), src, i < n ? 16 : 0);
+    }
+    auto load_block = [&](uint8_t *dst, const T *base, int kb) {
+        const long pg = bt[kb];
+        const T *blk = base + (pg * kv.kv_heads + kvh) * (long)kAttnPage * D;
+        for (int idx = tid; idx < kAttnPage * kCh; idx += 256) {
+            const int r = idx / kCh, c = idx % kCh;
+            const bool ok = kb * kAttnPage + r < nkeys;  // unwritten keys arrive as zeros
+            cp_async16(dst + swz<D>(r, c), blk + (long)r * D + c * 8, ok ? 16 : 0);
+        }
+    };
+    load_block(Ks, K, 0);
+    cp_async_commit();
+
+    uint32_t qa[D / 16][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    // scores of one block: c[nt][i]: n-tile nt (8 keys), i: (row g | g + 8) x (key 2t | 2t + 1)
+    auto scores = [&](const uint8_t *kt, float (&c)[8][4]) {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) c[nt][i] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+#pragma unroll
+            for (int n2 = 0; n2 < 4; ++n2) {
+                uint32_t b0, b1, b2, b3;
+                const int key = n2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+                ldsm_x4(smem_u32(kt + swz<D>(key, 2 * kk + ((lane >> 3) & 1))), b0, b1, b2, b3);
+                mma16<T>(c[2 * n2], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+                mma16<T>(c[2 * n2 + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
+            }
+    };
+
+    // ---- pass 1: row max and softmax sum
+    for (int kb = 0; kb < nb; ++kb) {
+        if (kb + 1 < nb) {
+            load_block(Ks + ((kb + 1) & 1) * kTile, K, kb + 1);
+            cp_async_commit();
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (kb == 0) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+                ldsm_x4(smem_u32(Qs + swz<D>(warp * 16 + (lane & 15), 2 * kk + (lane >> 4))), qa[kk][0], qa[kk][1],
+                        qa[kk][2], qa[kk][3]);
+        }
+        if (kb * kAttnPage <= wpos_max) {
+            float c[8][4];
+            scores(Ks + (kb & 1) * kTile, c);
+            float bm0 = -INFINITY, bm1 = -INFINITY;
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int key = kb * kAttnPage + nt * 8 + 2 * t + (i & 1);
+                    const bool hi = i >= 2;
+                    const float sv = key <= (hi ? pos1 : pos0) ? round_to<T>(c[nt][i]) * scale : -INFINITY;
+                    c[nt][i] = sv;
+                    if (hi)
+                        bm1 = fmaxf(bm1, sv);
+                    else
+                        bm0 = fmaxf(bm0, sv);
+                }
+#pragma unroll
+            for (int o = 1; o < 4; o <<= 1) {
+                bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, o));
+                bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, o));
+            }
+            const float n0 = fmaxf(m0, bm0), n1 = fmaxf(m1, bm1);
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                s0 += expf(c[nt][0] - n0) + expf(c[nt][1] - n0);
+                s1 += expf(c[nt][2] - n1) + expf(c[nt][3] - n1);
+            }
+            // rows with no key in this block keep their state (n = -inf only before any key)
+            if (n0 != -INFINITY) {
+                l0 = (m0 == -INFINITY ? 0.f : l0 * expf(m0 - n0)) + s0;
+                m0 = n0;
+            }
+            if (n1 != -INFINITY) {
+                l1 = (m1 == -INFINITY ? 0.f : l1 * expf(m1 - n1)) + s1;
+                m1 = n1;
+            }
+        }
+        __syncthreads();  // the stage is refilled next
+    }
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+
+    // ---- pass 2: probabilities and O = P . V
+    float o[D / 8][4];
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[dt][i] = 0.f;
+    load_block(Ks, K, 0);
+    load_block(Vs, V, 0);
+    cp_async_commit();
+    for (int kb = 0; kb < nb; ++kb) {
+        if (kb + 1 < nb) {
+            load_block(Ks + ((kb + 1) & 1) * kTile, K, kb + 1);
+            load_block(Vs + ((kb + 1) & 1) * kTile, V, kb + 1);
+            cp_async_commit();
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (kb * kAttnPage <= wpos_max) {
+            float c[8][4];
+            scores(Ks + (kb & 1) * kTile, c);
+            uint32_t pa[4][4];  // P as the A operand of four 16-key slices
+#pragma unroll
+            for (int nt = 0; nt < 8; ++nt) {
+                float pv[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int key = kb * kAttnPage + nt * 8 + 2 * t + (i & 1);
+                    const bool hi = i >= 2;
+                    pv[i] = 0.f;
+                    if (key <= (hi ? pos1 : pos0)) {
+                        const float e = expf(round_to<T>(c[nt][i]) * scale - (hi ? m1 : m0));
+                        pv[i] = round_to<T>(e) * (hi ? inv1 : inv0);
+                    }
+                }
+                pa[nt >> 1][(nt & 1) * 2 + 0] = pack_t2<T>(pv[0], pv[1]);
+                pa[nt >> 1][(nt & 1) * 2 + 1] = pack_t2<T>(pv[2], pv[3]);
+            }
+            const uint8_t *vt = Vs + (kb & 1) * kTile;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+                for (int d2 = 0; d2 < D / 16; ++d2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(smem_u32(vt + swz<D>(ks * 16 + (lane & 15), 2 * d2 + (lane >> 4))), b0, b1, b2, b3);
+                    // A: (row g, keys 2t..) (row g + 8, keys 2t..) (row g, keys 8 + 2t..) (row g + 8, keys 8 + 2t..)
+                    mma16<T>(o[2 * d2], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b0, b1);
+                    mma16<T>(o[2 * d2 + 1], pa[ks][0], pa[ks][1], pa[ks][2], pa[ks][3], b2, b3);
+                }
+        }
+        __syncthreads();
+    }
+    // O rows g, g + 8: T(o); position-major rows -> (position, head)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int r = h ? r1 : r0;
+        const int i = i0 + r / G;
+        if (i >= n) continue;
+        T *orow = out + ((long)b * n + i) * out_rs + (long)(kvh * G + r % G) * D;
+#pragma unroll
+        for (int dt = 0; dt < D / 8; ++dt)
+            *reinterpret_cast<uint32_t *>(orow + dt * 8 + 2 * t) = pack_t2<T>(o[dt][2 * h], o[dt][2 * h + 1]);
+    }
+}
+
+template <typename T, int D>
+void launch_prefill(T *out, long out_rs, const T *q, long q_rs, int batch, int n, int P, const KVPaged &kv, int G,
+                    cudaStream_t s) {
+    const size_t smem = (size_t)kPfRows * D * 2 + 4 * (size_t)kAttnPage * D * 2;
+    auto kern = attn_prefill_kernel<T, D>;
+    static bool configured = false;
+    if (!configured) {
+        WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        configured = true;
+    }
+    const int QP = kPfRows / G;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((n + QP - 1) / QP, kv.kv_heads, batch);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = g_rt.pdl ? 1 : 0;
+    const float scale = 1.0f / sqrtf((float)D);
+    WK_CHECK(cudaLaunchKernelEx(&cfg, kern, out, out_rs, q, q_rs, n, P, kv, G, scale));
+}
+
 }  // namespace
 
 template <typename T>
@@ -929,6 +1190,30 @@ template int attention_paged<__nv_bfloat16>(__nv_bfloat16 *, long, const __nv_bf
 template int attention_paged<float>(float *, long, const float *, long, const int *, const int *, int, int,
                                      const PagedKV &, int, cudaStream_t, bool, const void *, long, bool,
                                      const AttnSplitWs *);
+
+template <typename T>
+int attention_prefill_paged(T *out, long out_rs, const T *q, long q_rs, int batch, int n, int P, const PagedKV &c,
+                            int H, cudaStream_t s) {
+    if (batch <= 0 || n <= 0) return 0;
+    KVPaged kv{c.k, c.v, c.block_table, c.max_pages, c.page, c.kv_heads, c.hd};
+    const int G = H / c.kv_heads;
+    if constexpr (sizeof(T) == 2) {
+        if (c.page == kAttnPage && (G == 1 || G == 2 || G == 4 || G == 8) && (c.hd == 64 || c.hd == 128) &&
+            ((uintptr_t)c.k % 16) == 0 && ((uintptr_t)c.v % 16) == 0 && ((uintptr_t)q % 16) == 0 && (q_rs % 8) == 0 &&
+            ((uintptr_t)out % 4) == 0 && (out_rs % 2) == 0) {
+            if (c.hd == 64)
+                launch_prefill<T, 64>(out, out_rs, q, q_rs, batch, n, P, kv, G, s);
+            else
+                launch_prefill<T, 128>(out, out_rs, q, q_rs, batch, n, P, kv, G, s);
+            return 1;
+        }
+    }
+    return -1;  // the caller uses attention_paged
+}
+template int attention_prefill_paged<__half>(__half *, long, const __half *, long, int, int, int, const PagedKV &, int,
+                                             cudaStream_t);
+template int attention_prefill_paged<__nv_bfloat16>(__nv_bfloat16 *, long, const __nv_bfloat16 *, long, int, int, int,
+                                                    const PagedKV &, int, cudaStream_t);
 
 // Causal attention straight from fused QKV rows [B, T, (NH + 2 kvNH) HS]
 // (the layout cuda_gq_sdpa takes); out [B, T, NH HS].

@@ -314,7 +314,19 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             a.pf_bytes = capped(wbytes(d, col, c.wtype));
             launches += linear(a, rows, m->act, s, m->xn);
         }
-        {
+        // prefill: batch sequences of last_row_stride positions from 0, flash-style
+        int pf = -1;
+        if (rows > batch && rows == batch * last_row_stride) {
+            if (m->act == kF16)
+                pf = attention_prefill_paged<__half>((__half *)m->att, col, (const __half *)m->q, col, batch,
+                                                     last_row_stride, 0, kv, c.n_heads, s);
+            else
+                pf = attention_prefill_paged<__nv_bfloat16>((__nv_bfloat16 *)m->att, col,
+                                                            (const __nv_bfloat16 *)m->q, col, batch, last_row_stride,
+                                                            0, kv, c.n_heads, s);
+            if (pf > 0) launches += pf;
+        }
+        if (pf < 0) {
             // decode rows may split the context over several CTAs (split-K attention)
             const AttnSplitWs *ws = rows == batch ? &m->attn_ws : nullptr;
             if (m->act == kF16)

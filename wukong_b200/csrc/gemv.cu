@@ -434,8 +434,7 @@ __device__ void epilogue(const GemvArgs &a, const float *red, int tile, float &b
 // runs the same grid over the same tiles, so the CTA that owns a tile here
 // waits only for the CTA that owns it on each peer.  A wait that runs out
 // records code 42 and leaves the tile's x unchanged.
-template <typename T>
-__device__ void exchange_tile(const GemvArgs &a, const Smem &sm, int tile, const Side *pre) {
+__device__ void exchange_publish(const GemvArgs &a, const Smem &sm, int tile) {
     const int tid = threadIdx.x;
     const TpLink &L = a.tp;
     unsigned long long *e_s = reinterpret_cast<unsigned long long *>(sm.misc + 8 + 128);
@@ -458,6 +457,14 @@ __device__ void exchange_tile(const GemvArgs &a, const Smem &sm, int tile, const
         __threadfence_system();
         st_release_sys(reinterpret_cast<unsigned long long *>(L.peers[L.rank] + kXTileFlags) + tile, e);
     }
+}
+template <typename T>
+__device__ void exchange_finish(const GemvArgs &a, const Smem &sm, int tile, const Side *pre) {
+    const int tid = threadIdx.x;
+    const TpLink &L = a.tp;
+    const unsigned long long e = *reinterpret_cast<unsigned long long *>(sm.misc + 8 + 128);
+    int *ok_s = reinterpret_cast<int *>(sm.misc);
+    const size_t slot = ((size_t)(e & 1) * kTpMaxTiles + tile) * 128;
     if (tid < L.world &&
         !wait_flag(reinterpret_cast<const unsigned long long *>(L.peers[tid] + kXTileFlags) + tile, e, a.err, 42,
                    L.limit_ns))
@@ -709,9 +716,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         red[(g + 8) * 8 + 2 * t] = c[0][2] + c[1][2];
         red[(g + 8) * 8 + 2 * t + 1] = c[0][3] + c[1][3];
         __syncthreads();
-        if (a.epi == EPI_ARESID)
-            exchange_tile<T>(a, sm, tile, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
-        else
+        if (a.epi == EPI_ARESID) {
+            exchange_publish(a, sm, tile);
+            tl.phase(5);  // first tile published
+            exchange_finish<T>(a, sm, tile, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
+        } else
             epilogue<T>(a, sm.red, tile, best_v, best_k, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
         __syncthreads();  // red is rewritten by the next tile
         tl.phase(3);          // first tile stored

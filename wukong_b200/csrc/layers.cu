@@ -287,10 +287,18 @@ void gqa_fused(void *out, const void *embeds, const float *freqs, const float *n
     }
     // one new row per sequence over a cached context: long contexts split over CTAs
     const AttnSplitWs *ws = r.cached && r.n == 1 && g_sess.ws.scores ? &g_sess.ws : nullptr;
-    if (act == kF16)
+    // several new rows per sequence (prefill, or a changed suffix): flash-style
+    int pf = -1;
+    if (r.n > 1)
+        pf = act == kF16 ? attention_prefill_paged<__half>((__half *)att, col, (const __half *)q, col, batch, r.n, r.P,
+                                                           kv, NH, stream())
+                         : attention_prefill_paged<__nv_bfloat16>((__nv_bfloat16 *)att, col,
+                                                                  (const __nv_bfloat16 *)q, col, batch, r.n, r.P, kv,
+                                                                  NH, stream());
+    if (pf < 0 && act == kF16)
         attention_paged<__half>((__half *)att, col, (const __half *)q, col, seq, pos, rows, row, kv, NH, stream(), true,
                                 nullptr, 0, r.n == 1, ws);
-    else
+    else if (pf < 0)
         attention_paged<__nv_bfloat16>((__nv_bfloat16 *)att, col, (const __nv_bfloat16 *)q, col, seq, pos, rows, row,
                                        kv, NH, stream(), true, nullptr, 0, r.n == 1, ws);
     {

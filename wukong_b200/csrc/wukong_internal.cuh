@@ -195,6 +195,14 @@ int attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_o
                      const AttnSplitWs *ws = nullptr);
 template <typename T>
 void attention_qkv_rows(T *out, const T *qkv, int B, int Tn, int NH, int kvNH, int HS, cudaStream_t s);
+// Prefill rows: n positions P..P+n-1 of each of `batch` sequences (q row b n + i
+// is position P + i) over the paged cache, flash-style on tensor cores with
+// the reference's rounding points.  Returns 1 (launches), or -1 when the
+// shapes are not supported (16-bit K/V, 64-token pages, head_dim 64 / 128,
+// 1, 2, 4 or 8 query heads per KV head) and attention_paged must be used.
+template <typename T>
+int attention_prefill_paged(T *out, long out_rs, const T *q, long q_rs, int batch, int n, int P, const PagedKV &c,
+                            int H, cudaStream_t s);
 
 // ---------------------------------------------------------------- matmul.cu
 // out[M, N] = X[M, K] . W[N, K]^T (+bias), reference numerics; dispatches to the

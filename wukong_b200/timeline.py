@@ -19,6 +19,8 @@ its time goes (means over CTAs and launches, in microseconds):
           attention pages and query heads per KV head (split: pages, splits)
 
 Usage: python -m wukong_b200.timeline [--model 1b|8b] [--steps N] [--prompt P]
+       python -m torch.distributed.run --nproc-per-node N -m wukong_b200.timeline --model 8b
+           (tensor-parallel over N GPUs; all-reduce+resid p5: first tile published)
 """
 import argparse
 import ctypes
@@ -28,20 +30,35 @@ import sys
 import numpy as np
 
 SLOTS, BLOCKS, STAMPS = 1024, 320, 9
-KINDS = {0: "store", 1: "resid", 2: "qkv", 3: "swiglu", 4: "logits", 5: "partial", 100: "attention",
+KINDS = {0: "store", 1: "resid", 2: "qkv", 3: "swiglu", 4: "logits", 5: "partial", 6: "all-reduce+resid",
+         100: "attention",
          101: "attention scores (split)", 102: "attention P.V (split)"}
 
 
 def record(model="1b", steps=12, prompt=None, batch=1):
+    """Under torch.distributed.run with more than one rank the model is
+    tensor-parallel over the ranks (one per GPU); every rank records its own
+    launches."""
     import wukong_b200 as wk
     wk.LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libwukong_timeline.so")
     from wukong_b200.engine import LLAMA, Engine, SyntheticLlama
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
     L = wk.lib()
-    L.cuda_init(0)
+    L.cuda_init(int(os.environ.get("LOCAL_RANK", "0")))
+    if world > 1:
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        torch.distributed.init_process_group("gloo")
+        idbuf = ctypes.create_string_buffer(128)
+        if rank == 0:
+            wk.check(L.wk_tp_unique_id(idbuf))
+        t = torch.frombuffer(bytearray(idbuf.raw), dtype=torch.uint8)
+        torch.distributed.broadcast(t, 0)
+        wk.check(L.wk_tp_init(rank, world, bytes(t.numpy())))
     cfg = dict(LLAMA[model])
     P = prompt or (128 if model == "1b" else 2048)
-    sm = SyntheticLlama(cfg, P + steps + 16, seed=1234)
-    eng = Engine.from_synthetic(sm, max_batch=batch)
+    sm = SyntheticLlama(cfg, P + steps + 16, seed=1234, tp_rank=rank, tp_world=world)
+    eng = Engine.from_synthetic(sm, max_batch=batch, tp=world > 1)
     ids = np.random.default_rng(7).integers(0, cfg["V"], size=(batch, P)).astype(np.int32)
     d = L.cuda_malloc(ids.nbytes)
     L.cuda_to_device(d, ids.ctypes.data_as(ctypes.c_void_p), ids.nbytes)
@@ -60,6 +77,8 @@ def record(model="1b", steps=12, prompt=None, batch=1):
     lps = eng.launches_per_step()
     eng.destroy()
     L.cuda_free(d)
+    if world > 1:
+        L.wk_tp_fini()
     return info, stamps.astype(np.int64), n, res, lps
 
 
@@ -106,6 +125,8 @@ def main(argv=None):
     ap.add_argument("--prompt", type=int, default=None)
     a = ap.parse_args(argv)
     info, stamps, n, res, lps = record(a.model, a.steps, a.prompt)
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
     rows, span_us, nev = summarize(info, stamps, n)
     print(f"model {a.model}: {nev} GEMV / attention launches recorded over {span_us:.1f} us ({a.steps} decode "
           f"steps of {lps} launches; %globaltimer step {res} ns)")
