@@ -211,6 +211,92 @@ __device__ __forceinline__ void store_out(const GemmArgs &a, int n, int m, float
     }
 }
 
+// Vectorised epilogue of 8 consecutive output rows n..n+7 (a 16-byte group)
+// for one token m: the same formulas and rounding points as store_out.
+template <typename T>
+__device__ __forceinline__ void store_out8(const GemmArgs &a, int n, int m, const float (&v)[8], const float *gate) {
+    switch (a.epi) {
+    case EPI_STORE: {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = v[j];
+        if (a.bias) {
+            const uint4 b = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(a.bias) + n);
+            const T *bt = reinterpret_cast<const T *>(&b);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] += to_float(bt[j]);
+        }
+        uint4 u;
+        T *ut = reinterpret_cast<T *>(&u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ut[j] = from_float<T>(o[j]);
+        *reinterpret_cast<uint4 *>(reinterpret_cast<T *>(a.out) + (long)m * a.ldo + n) = u;
+        break;
+    }
+    case EPI_PARTIAL: {
+        float4 *o = reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.out) + (long)m * a.ldo + n);
+        o[0] = make_float4(v[0], v[1], v[2], v[3]);
+        o[1] = make_float4(v[4], v[5], v[6], v[7]);
+        break;
+    }
+    case EPI_RESID: {
+        const uint4 r = *reinterpret_cast<const uint4 *>(reinterpret_cast<const T *>(a.res) + (long)m * a.ldr + n);
+        const T *rt = reinterpret_cast<const T *>(&r);
+        uint4 u;
+        T *ut = reinterpret_cast<T *>(&u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ut[j] = from_float<T>(to_float(rt[j]) + round_to<T>(v[j]));
+        *reinterpret_cast<uint4 *>(reinterpret_cast<T *>(a.out) + (long)m * a.ldo + n) = u;
+        break;
+    }
+    case EPI_QKV: {
+        const int pos = a.pos[m];
+        uint4 u;
+        T *ut = reinterpret_cast<T *>(&u);
+        const bool rope = n < a.nq + a.nk;
+        const int base = n < a.nq ? 0 : (rope ? a.nq : a.nq + a.nk);
+        const int dd = (n - base) % a.hd;  // group start within its head (the 8 rows share the head)
+        if (rope) {
+            const float *f = a.freqs + (long)pos * a.hd + dd;
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+                const float y0 = round_to<T>(v[j]), y1 = round_to<T>(v[j + 1]);
+                const float cs = f[j], sn = f[j + 1];
+                ut[j] = from_float<T>(y0 * cs - y1 * sn);
+                ut[j + 1] = from_float<T>(y0 * sn + y1 * cs);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ut[j] = from_float<T>(v[j]);
+        }
+        if (n < a.nq) {
+            *reinterpret_cast<uint4 *>(reinterpret_cast<T *>(a.out) + (long)m * a.ldo + n) = u;
+        } else {
+            const int h = (n - base) / a.hd;
+            const long page = a.block_table[(long)a.seq[m] * a.max_pages + pos / a.page];
+            T *pool = reinterpret_cast<T *>(rope ? a.kpool : a.vpool);
+            *reinterpret_cast<uint4 *>(pool + ((page * a.kv_heads + h) * a.page + pos % a.page) * a.hd + dd) = u;
+        }
+        break;
+    }
+    case EPI_SWIGLU: {
+        uint4 u;
+        T *ut = reinterpret_cast<T *>(&u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float up = round_to<T>(v[j]);
+            const float g = round_to<T>(gate[j]);
+            const float sig = 1.0f / (1.0f + expf(-g));
+            ut[j] = from_float<T>((g * sig) * up);
+        }
+        *reinterpret_cast<uint4 *>(reinterpret_cast<T *>(a.out) + (long)m * a.ldo + n) = u;
+        break;
+    }
+    default:
+        break;
+    }
+}
+
 template <typename T, int WT, int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
     using L = Layout<BN>;
@@ -374,7 +460,43 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         const bool acc_ok = ok && mbar_wait_bounded(&bars->acc_full, 0, err, 16);
         tc_fence_after();
         float *xchg = reinterpret_cast<float *>(RAW);  // [128 rows][32 columns] for row pairing
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        if (a.vec) {
+            // the accumulators of 32 tokens go through shared memory ([32 tokens][128 rows]
+            // fp32) so that each thread then handles 16-byte groups of 8 consecutive outputs
+            float *st = reinterpret_cast<float *>(RAW);
+            const int te = threadIdx.x - 64;  // 0..127 over warps 2..5
+            const int groups = swiglu ? 8 : 16;  // 8-row groups per token (SwiGLU: the 64 up rows)
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t v[32];
+                tc_ld32(tmem + (((uint32_t)(warp & 3) * 32) << 16) + (uint32_t)c0, v);
+                if (!acc_ok)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = 0u;
+                asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous chunk's groups are done
+#pragma unroll
+                for (int i = 0; i < 32; ++i) st[i * 128 + row] = __uint_as_float(v[i]);
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                for (int it = te; it < 32 * groups; it += 128) {
+                    const int i = it / groups, r0 = (it % groups) * 8;
+                    const int m = m0 + c0 + i;
+                    const int n = swiglu ? n_tile * 64 + r0 : n_tile * 128 + r0;
+                    if (m >= a.M || n >= (swiglu ? a.F : a.N)) continue;
+                    float vv[8], gg[8];
+                    const float4 *src = reinterpret_cast<const float4 *>(st + i * 128 + r0);
+                    const float4 x0 = src[0], x1 = src[1];
+                    vv[0] = x0.x, vv[1] = x0.y, vv[2] = x0.z, vv[3] = x0.w;
+                    vv[4] = x1.x, vv[5] = x1.y, vv[6] = x1.z, vv[7] = x1.w;
+                    if (swiglu) {
+                        const float4 *gs = reinterpret_cast<const float4 *>(st + i * 128 + 64 + r0);
+                        const float4 y0 = gs[0], y1 = gs[1];
+                        gg[0] = y0.x, gg[1] = y0.y, gg[2] = y0.z, gg[3] = y0.w;
+                        gg[4] = y1.x, gg[5] = y1.y, gg[6] = y1.z, gg[7] = y1.w;
+                    }
+                    store_out8<T>(a, n, m, vv, gg);
+                }
+            }
+        }
+        for (int c0 = 0; !a.vec && c0 < BN; c0 += 32) {
             uint32_t v[32];
             const uint32_t taddr = tmem + (((uint32_t)(warp & 3) * 32) << 16) + (uint32_t)c0;
             tc_ld32(taddr, v);
@@ -471,6 +593,15 @@ void gemm_tc(GemmArgs a, int act, cudaStream_t s) {
                                                      (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
             WK_PANIC("gemm_tc: weight tensor map");
     }
+    // 16-byte groups of outputs when every row the epilogue touches is 16-byte aligned
+    auto al16 = [](const void *p, long ld, size_t esz) {
+        return p == nullptr || (((uintptr_t)p % 16) == 0 && ((size_t)ld * esz) % 16 == 0);
+    };
+    a.vec = (a.epi == EPI_SWIGLU ? a.F % 8 == 0 : a.N % 8 == 0) &&
+            al16(a.out, a.ldo, a.epi == EPI_PARTIAL ? 4 : es) && (a.epi != EPI_RESID || al16(a.res, a.ldr, es)) &&
+            (a.epi != EPI_STORE || al16(a.bias, 0, es)) &&
+            (a.epi != EPI_QKV || (a.hd % 8 == 0 && a.nq % 8 == 0 && a.nk % 8 == 0 && al16(a.kpool, 0, es) &&
+                                  al16(a.vpool, 0, es)));
     const bool pdl = g_rt.pdl && a.pdl;
 #define WK_TC_LAUNCH(T, W)                        \
     do {                                          \

@@ -149,6 +149,7 @@ struct GemmArgs {
     int F = 0;
     int *err = nullptr;
     int pdl = 1;
+    int vec = 0;  // set by gemm_tc(): the epilogue stores 8 outputs (16 bytes) per access
 };
 bool gemm_tc_supported(int wtype, int act, int K, int N, int epi, int F);
 void gemm_tc(GemmArgs a, int act, cudaStream_t s);
