@@ -426,101 +426,136 @@ __device__ void epilogue(const GemvArgs &a, const float *red, int tile, float &b
     }
 }
 
-// ARESID epilogue of one tile (all threads of the CTA take part): the tile's
-// fp32 partial sums go to this rank's exchange buffer, the tile's flag is
-// published, and once every rank has published the same tile the sum over
-// ranks (in rank order, so every rank computes the same x) is rounded and
-// added to the residual: x = T(x + T(sum)), the RESID formula.  Every rank
-// runs the same grid over the same tiles, so the CTA that owns a tile here
-// waits only for the CTA that owns it on each peer.  A wait that runs out
-// records code 42 and leaves the tile's x unchanged.
-__device__ void exchange_publish(const GemvArgs &a, const Smem &sm, int tile) {
+// ARESID epilogue of one tile (all threads of the CTA take part): thread
+// (row r, column m) pushes its fp32 partial sum, with the call's epoch for the
+// tile, into every peer's buffer as one 8-byte word, then polls its own buffer
+// until every peer's word for this (tile, r, m) carries the same epoch, adds
+// the partials in rank order (so every rank computes the same x) and stores
+// x = T(x + T(sum)), the RESID formula.  Payload slots alternate with the
+// epoch's parity; a slot is rewritten two calls later, after every peer has
+// pushed the call in between, which it does only once it has read this one.
+// A wait that runs out records code 42 and leaves that output unchanged.
+__device__ __forceinline__ void st_u64_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_u64_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ll_word(uint32_t bits, unsigned long long e) {
+    return ((unsigned long long)(uint32_t)e << 32) | bits;
+}
+// Poll *p until its epoch half equals e; the value half, or false after limit_ns.
+__device__ __forceinline__ bool ll_wait(const unsigned long long *p, unsigned long long e, uint32_t &bits,
+                                        unsigned long long limit_ns) {
+    unsigned long long v = ld_u64_sys(p);
+    if ((uint32_t)(v >> 32) != (uint32_t)e) {
+        const uint64_t t0 = globaltimer_ns();
+        do {
+            if (globaltimer_ns() - t0 > limit_ns) return false;
+            v = ld_u64_sys(p);
+        } while ((uint32_t)(v >> 32) != (uint32_t)e);
+    }
+    bits = (uint32_t)v;
+    return true;
+}
+
+template <typename T>
+__device__ void exchange_tile(const GemvArgs &a, const Smem &sm, int tile, const Side *pre, Timeline &tl) {
     const int tid = threadIdx.x;
     const TpLink &L = a.tp;
     unsigned long long *e_s = reinterpret_cast<unsigned long long *>(sm.misc + 8 + 128);
-    int *ok_s = reinterpret_cast<int *>(sm.misc);
     if (tid == 0) {
         const unsigned long long e = L.tile_epoch[tile] + 1;
         L.tile_epoch[tile] = e;
         *e_s = e;
-        *ok_s = 1;
     }
     __syncthreads();
     const unsigned long long e = *e_s;
-    const size_t slot = ((size_t)(e & 1) * kTpMaxTiles + tile) * 128;
+    // word (parity, tile, source rank, tid) of a receiver's buffer
+    const size_t base = ((size_t)(e & 1) * kTpMaxTiles + tile) * kTpMaxWorld * 128 + tid;
+    float own = 0.f;
     if (tid < 128) {
-        const int r = tid >> 3, m = tid & 7;
-        reinterpret_cast<float *>(L.peers[L.rank] + kXTilePay)[slot + tid] = tile_sum(sm.red, r, m);
+        own = tile_sum(sm.red, tid >> 3, tid & 7);
+        const unsigned long long w = ll_word(__float_as_uint(own), e);
+        for (int q = 0; q < L.world; ++q)
+            if (q != L.rank)
+                st_u64_sys(reinterpret_cast<unsigned long long *>(L.peers[q] + kXTileLL) + base + L.rank * 128, w);
     }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence_system();
-        st_release_sys(reinterpret_cast<unsigned long long *>(L.peers[L.rank] + kXTileFlags) + tile, e);
-    }
-}
-template <typename T>
-__device__ void exchange_finish(const GemvArgs &a, const Smem &sm, int tile, const Side *pre) {
-    const int tid = threadIdx.x;
-    const TpLink &L = a.tp;
-    const unsigned long long e = *reinterpret_cast<unsigned long long *>(sm.misc + 8 + 128);
-    int *ok_s = reinterpret_cast<int *>(sm.misc);
-    const size_t slot = ((size_t)(e & 1) * kTpMaxTiles + tile) * 128;
-    if (tid < L.world &&
-        !wait_flag(reinterpret_cast<const unsigned long long *>(L.peers[tid] + kXTileFlags) + tile, e, a.err, 42,
-                   L.limit_ns))
-        *ok_s = 0;
-    __syncthreads();
-    const bool ok = *ok_s != 0;
-    __syncthreads();  // ok_s / e_s are rewritten by the next tile
-    if (!ok || tid >= 128) return;
+    tl.phase(5);  // first tile pushed
+    __syncthreads();  // e_s is rewritten by the next tile
+    if (tid >= 128) return;
     const int r = tid >> 3, m = tid & 7;
-    if (m >= a.M || !row_valid(a, tile, r)) return;
-    const int n = tile_row(a, tile, r);
+    const bool valid = m < a.M && row_valid(a, tile, r);
+    const unsigned long long *mine = reinterpret_cast<const unsigned long long *>(L.peers[L.rank] + kXTileLL) + base;
     float acc = 0.f;
-    for (int q = 0; q < L.world; ++q) acc += __ldcv(reinterpret_cast<const float *>(L.peers[q] + kXTilePay) + slot + tid);
+    bool ok = true;
+    for (int q = 0; q < L.world; ++q) {
+        if (q == L.rank) {
+            acc += own;
+            continue;
+        }
+        uint32_t bits = 0;
+        if (!ll_wait(mine + q * 128, e, bits, L.limit_ns)) {
+            ok = false;
+            break;
+        }
+        acc += __uint_as_float(bits);
+    }
+    if (!ok) {
+        atomicCAS(a.err, 0, 42);
+        return;
+    }
+    if (!valid) return;
+    const int n = tile_row(a, tile, r);
     const float res = pre ? pre->s0 : to_float(reinterpret_cast<const T *>(a.res)[(long)m * a.ldr + n]);
     reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(res + round_to<T>(acc));
 }
 
 // The logits winners of a vocabulary shard (tid < M hold this rank's best
-// value and order key of row tid) exchanged with every rank by the last CTA;
+// value and order key of row tid) exchanged with every rank by the last CTA,
+// in the same push protocol (three words per row: value, key low, key high);
 // the best over ranks in the reference argmax's tie order gives the token.
 // All threads of the CTA call it.
-__device__ void exchange_winners(const GemvArgs &a, float *sv, uint64_t *sk, float bv, uint64_t bk) {
+__device__ void exchange_winners(const GemvArgs &a, float bv, uint64_t bk) {
     const int tid = threadIdx.x;
     const TpLink &L = a.tp;
     __shared__ unsigned long long e_w;
-    __shared__ int ok_w;
     if (tid == 0) {
         e_w = *L.win_epoch + 1;
         *L.win_epoch = e_w;
-        ok_w = 1;
     }
     __syncthreads();
+    if (tid >= a.M) return;
     const unsigned long long e = e_w;
-    const int par = (int)(e & 1);
-    uint8_t *mine = L.peers[L.rank] + kXWinPay + par * kXWinSlot;
-    if (tid < a.M) {
-        reinterpret_cast<unsigned long long *>(mine)[tid] = bk;
-        reinterpret_cast<float *>(mine + 8L * a.M)[tid] = bv;
+    // word (parity, source rank, row, j) of a receiver's buffer
+    auto slot = [&](int src) { return ((size_t)(e & 1) * kTpMaxWorld + src) * 32 + tid * 4; };
+    const unsigned long long w0 = ll_word(__float_as_uint(bv), e), w1 = ll_word((uint32_t)bk, e),
+                             w2 = ll_word((uint32_t)(bk >> 32), e);
+    for (int q = 0; q < L.world; ++q) {
+        if (q == L.rank) continue;
+        unsigned long long *d = reinterpret_cast<unsigned long long *>(L.peers[q] + kXWinLL) + slot(L.rank);
+        st_u64_sys(d, w0);
+        st_u64_sys(d + 1, w1);
+        st_u64_sys(d + 2, w2);
     }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence_system();
-        st_release_sys(reinterpret_cast<unsigned long long *>(L.peers[L.rank] + kXWinFlags) + par, e);
-    }
-    if (tid < L.world &&
-        !wait_flag(reinterpret_cast<const unsigned long long *>(L.peers[tid] + kXWinFlags) + par, e, a.err, 43,
-                   L.limit_ns))
-        ok_w = 0;
-    __syncthreads();
-    if (!ok_w || tid >= a.M) return;
     float best_v = -INFINITY;
     uint64_t best_k = ~0ull;
+    const unsigned long long *mine = reinterpret_cast<const unsigned long long *>(L.peers[L.rank] + kXWinLL);
     for (int q = 0; q < L.world; ++q) {
-        const uint8_t *rec = L.peers[q] + kXWinPay + par * kXWinSlot;
-        const uint64_t k = __ldcv(reinterpret_cast<const unsigned long long *>(rec) + tid);
-        const float v = __ldcv(reinterpret_cast<const float *>(rec + 8L * a.M) + tid);
+        float v = bv;
+        uint64_t k = bk;
+        if (q != L.rank) {
+            uint32_t b0 = 0, b1 = 0, b2 = 0;
+            if (!ll_wait(mine + slot(q), e, b0, L.limit_ns) || !ll_wait(mine + slot(q) + 1, e, b1, L.limit_ns) ||
+                !ll_wait(mine + slot(q) + 2, e, b2, L.limit_ns)) {
+                atomicCAS(a.err, 0, 43);
+                return;
+            }
+            v = __uint_as_float(b0);
+            k = ((uint64_t)b2 << 32) | b1;
+        }
         if (k == ~0ull) continue;
         if (v > best_v || (v == best_v && k < best_k)) {
             best_v = v;
@@ -528,8 +563,6 @@ __device__ void exchange_winners(const GemvArgs &a, float *sv, uint64_t *sk, flo
         }
     }
     a.tokens[tid] = logits_index(best_k, a.pack);
-    (void)sv;
-    (void)sk;
 }
 
 // Epilogue of a tile owned by one warp (SwiGLU or logits): lane (g, t) has
@@ -716,11 +749,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         red[(g + 8) * 8 + 2 * t] = c[0][2] + c[1][2];
         red[(g + 8) * 8 + 2 * t + 1] = c[0][3] + c[1][3];
         __syncthreads();
-        if (a.epi == EPI_ARESID) {
-            exchange_publish(a, sm, tile);
-            tl.phase(5);  // first tile published
-            exchange_finish<T>(a, sm, tile, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
-        } else
+        if (a.epi == EPI_ARESID)
+            exchange_tile<T>(a, sm, tile, pre && tile == (int)blockIdx.x ? &side0 : nullptr, tl);
+        else
             epilogue<T>(a, sm.red, tile, best_v, best_k, pre && tile == (int)blockIdx.x ? &side0 : nullptr);
         __syncthreads();  // red is rewritten by the next tile
         tl.phase(3);          // first tile stored
@@ -807,7 +838,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
                 }
             }
             if (tid == 0) *a.counter = 0;
-            if (a.tp.world > 1 && a.tokens) exchange_winners(a, sv, sk, bv, bk);
+            if (a.tp.world > 1 && a.tokens) exchange_winners(a, bv, bk);
         }
     }
 }

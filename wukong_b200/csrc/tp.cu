@@ -106,7 +106,7 @@ constexpr size_t kWinSlot = kXWinSlot;
 constexpr size_t kP2POff = kXArPay;
 constexpr size_t kP2PBytes = kXBytes;
 constexpr int kMaxWorld = 8;
-static_assert(kXArPay + 2 * kXArSlot == kXWinPay, "exchange layout");
+static_assert(kXArPay + 2 * kXArSlot == kXWinPay && kMaxWorld == kTpMaxWorld, "exchange layout");
 
 struct P2P {
     bool ok = false;
@@ -465,17 +465,20 @@ int wk_tp_gemv_selftest(int world, int N, int K, int M) {
     if (rc == 0 && (wk_fill_random_q8_0(w, N, K, 101, 0.02f) || wk_fill_random_f16(x, (long)M * K, 102, 1.0f) ||
                     wk_fill_random_f16(res, (long)M * N, 103, 1.0f)))
         rc = -1;
-    // the emulated ranks q = 1..world-1 published every tile of their first call (epoch 1,
-    // slot parity 1) with the partial sums 0.25 q
+    // the emulated ranks q = 1..world-1 pushed every tile of their first call (epoch 1,
+    // slot parity 1) to rank 0, with the partial sums 0.25 q
     if (rc == 0) {
-        std::vector<float> pay((size_t)N / 16 * 128);
-        std::vector<unsigned long long> flags(N / 16, 1ull);
-        for (int q = 1; q < world; ++q) {
-            for (size_t i = 0; i < pay.size(); ++i) pay[i] = 0.25f * q;
-            ok(cudaMemcpy(bufs[q] + kXTilePay + (size_t)kTpMaxTiles * 512, pay.data(), pay.size() * 4,
-                          cudaMemcpyHostToDevice));
-            ok(cudaMemcpy(bufs[q] + kXTileFlags, flags.data(), flags.size() * 8, cudaMemcpyHostToDevice));
-        }
+        std::vector<unsigned long long> words((size_t)N / 16 * kTpMaxWorld * 128, 0ull);
+        for (int t = 0; t < N / 16; ++t)
+            for (int q = 1; q < world; ++q)
+                for (int i = 0; i < 128; ++i) {
+                    const float v = 0.25f * q;
+                    uint32_t bits;
+                    memcpy(&bits, &v, 4);
+                    words[((size_t)t * kTpMaxWorld + q) * 128 + i] = (1ull << 32) | bits;
+                }
+        ok(cudaMemcpy(bufs[0] + kXTileLL + (size_t)kTpMaxTiles * kTpMaxWorld * 128 * 8, words.data(), words.size() * 8,
+                      cudaMemcpyHostToDevice));
     }
     std::vector<__half> h_res((size_t)M * N), h_out((size_t)M * N);
     std::vector<float> h_p((size_t)M * N);

@@ -42,9 +42,15 @@ constexpr size_t kXArPay = 512;                              // [2][kXArSlot] fp
 constexpr size_t kXArSlot = 256 * 1024;
 constexpr size_t kXWinPay = kXArPay + 2 * kXArSlot;          // [2][kXWinSlot] winners: keys u64 [B], values f32 [B]
 constexpr size_t kXWinSlot = 4096;
-constexpr size_t kXTileFlags = kXWinPay + 2 * kXWinSlot;     // [kTpMaxTiles] u64: epoch of each tile's last publish
-constexpr size_t kXTilePay = kXTileFlags + 8 * kTpMaxTiles;  // [2][kTpMaxTiles][16 rows][8 columns] fp32
-constexpr size_t kXBytes = kXTilePay + 2 * (size_t)kTpMaxTiles * 512;
+// Decode exchanges of the GEMV epilogues are pushed, not pulled: a rank
+// stores each value together with the call's epoch in one 8-byte word
+// (value bits low, epoch high) into every peer's buffer, and a receiver polls
+// its own words until the epoch matches -- one NVLink write per value and no
+// system-scope fence or separate flag (single-copy atomic 8-byte stores).
+constexpr int kTpMaxWorld = 8;
+constexpr size_t kXTileLL = kXWinPay + 2 * kXWinSlot;  // [2][kTpMaxTiles][kTpMaxWorld src][128] u64
+constexpr size_t kXWinLL = kXTileLL + 2 * (size_t)kTpMaxTiles * kTpMaxWorld * 128 * 8;  // [2][src][8 rows][4] u64
+constexpr size_t kXBytes = kXWinLL + 2 * (size_t)kTpMaxWorld * 8 * 4 * 8;
 
 // What a kernel needs to exchange with the other ranks (device pointers).
 struct TpLink {
