@@ -806,12 +806,296 @@ __global__ void __launch_bounds__(128) attn_split_pv_kernel(T *__restrict__ out,
     tl.phase(2);  // combined
 }
 
+// Both split-K passes in one launch: every split CTA computes its scores and
+// its (max, sum) pair, publishes the pair and waits (bounded) until all splits
+// of its (row, head) have published -- the grid is launched only when it fits
+// on the GPU at once, so every split is resident -- then forms M and the sum
+// itself from the pairs in split order (the same values the two-launch path's
+// last CTA computes), turns its own scores (kept in shared memory) into P and
+// multiplies its V pages, which it requested while waiting.  The last CTA of
+// the (row, head) adds the partials in split order.  Same arithmetic, one
+// dependent hand-over fewer, and no round trip of the scores through memory.
 template <typename T, int D>
-bool launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
+__global__ void __launch_bounds__(128) attn_split_fused_kernel(T *__restrict__ out, long out_rs, const T *__restrict__ q,
+                                                               long q_rs, const int *__restrict__ seq_of_row,
+                                                               const int *__restrict__ pos_of_row, KVPaged kv, int G,
+                                                               int pps, float scale, float *__restrict__ mpart,
+                                                               float *__restrict__ opart, int *__restrict__ counter,
+                                                               int *__restrict__ counter_a, int *err, int early,
+                                                               unsigned long long limit_ns) {
+    Timeline tl;
+    constexpr int kPageBytes = kAttnPage * D * 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *ring = smem;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kAttnSlots * kPageBytes);
+    float *red = reinterpret_cast<float *>(bars + kAttnSlots);  // [8][4]
+    float *minv = red + 32;                                     // [8][2]: M, 1 / sum
+    T *qs = reinterpret_cast<T *>(minv + 16);                   // [8][D]
+    T *own = qs + 8 * D;                                        // [8][pps * 64] this split's scores, then P
+    __shared__ int last, ok_s;
+    const int kvh = blockIdx.x, row = blockIdx.y, z = blockIdx.z, nz = gridDim.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int seq = seq_of_row[row], pos = pos_of_row[row];
+    const int L = pos + 1;
+    const int npages = (L + kAttnPage - 1) / kAttnPage;
+    const int p0 = z * pps, p1 = min(p0 + pps, npages);
+    const int n = p1 > p0 ? p1 - p0 : 0;
+    const int wl = pps * kAttnPage;
+    const T *K = reinterpret_cast<const T *>(kv.k);
+    const T *V = reinterpret_cast<const T *>(kv.v);
+    const int *bt = kv.block_table + (long)seq * kv.max_pages;
+    const long pg_last = early && tid == 0 && n > 0 && p1 == npages ? bt[npages - 1] : -1;
+    // units 0..n-1: this split's K pages, n..2n-1: its V pages
+    auto page_src = [&](int i) -> const T * {
+        const int pi = i < n ? i : i - n;
+        const long pg = pg_last >= 0 && p0 + pi == npages - 1 ? pg_last : bt[p0 + pi];
+        return (i < n ? K : V) + (pg * kv.kv_heads + kvh) * (long)kAttnPage * D;
+    };
+    if (tid < kAttnSlots) mbar_init(bars + tid, 1);
+    mbar_fence_init();
+    __syncthreads();
+    int issued = 0;
+    if (tid == 0 && early)  // decode: pages before the newest one were written by earlier launches
+        for (; issued < kAttnSlots && issued < n && p0 + issued < npages - 1; ++issued) {
+            mbar_expect_tx(bars + issued, kPageBytes);
+            bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
+        }
+    pdl_wait();
+    pdl_trigger();
+    tl.mark(103, npages, nz);
+    if (tid == 0)
+        for (; issued < kAttnSlots && issued < 2 * n; ++issued) {
+            mbar_expect_tx(bars + issued, kPageBytes);
+            bulk_g2s(ring + issued * kPageBytes, page_src(issued), kPageBytes, bars + issued);
+        }
+    const T *qrow = q + (long)row * q_rs + (long)kvh * G * D;
+    stage_q<T, D>(qs, qrow, G);
+    __syncthreads();
+    uint32_t qb[D / 16][2];
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+        qb[kk][0] = *reinterpret_cast<const uint32_t *>(qs + g * D + kk * 16 + 2 * t);
+        qb[kk][1] = *reinterpret_cast<const uint32_t *>(qs + g * D + kk * 16 + 2 * t + 8);
+    }
+    // ---- scores of this split's keys, rounded to T, and the split's max per head
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+    bool ok = true;
+    int consumed = 0;
+    for (int i = 0; i < n; ++i, ++consumed) {
+        const int slot = consumed % kAttnSlots;
+        if (!mbar_wait_bounded(bars + slot, (consumed / kAttnSlots) & 1, err, 4)) ok = false;
+        const T *kt = reinterpret_cast<const T *>(ring + slot * kPageBytes) + warp * 16 * D;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ok) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(smem_u32(kt + (lane & 15) * D + kk * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
+                mma16<T>(c, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+            }
+        }
+        const int k0 = (p0 + i) * kAttnPage + warp * 16 + g;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int key = k0 + (j >> 1) * 8, h = 2 * t + (j & 1);
+            const float sv = key < L ? round_to<T>(c[j]) : -INFINITY;
+            own[h * wl + key - p0 * kAttnPage] = from_float<T>(key < L ? sv : 0.f);
+            if (j & 1)
+                mx1 = fmaxf(mx1, sv * scale);
+            else
+                mx0 = fmaxf(mx0, sv * scale);
+        }
+        __syncthreads();  // the slot is free: request the next page (K, then this split's V pages)
+        if (tid == 0 && issued < 2 * n) {
+            const int sl = issued % kAttnSlots;
+            mbar_expect_tx(bars + sl, kPageBytes);
+            bulk_g2s(ring + sl * kPageBytes, page_src(issued), kPageBytes, bars + sl);
+            ++issued;
+        }
+    }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    if (g == 0) {
+        red[(2 * t) * 4 + warp] = mx0;
+        red[(2 * t + 1) * 4 + warp] = mx1;
+    }
+    __syncthreads();
+    const long rh = (long)row * kv.kv_heads + kvh;
+    __shared__ float s_m[8];
+    if (tid < 8) s_m[tid] = fmaxf(fmaxf(red[tid * 4], red[tid * 4 + 1]), fmaxf(red[tid * 4 + 2], red[tid * 4 + 3]));
+    __syncthreads();
+    {
+        const int h = tid >> 4, i0 = tid & 15;  // 16 threads per head, keys i0, i0 + 16, ...
+        const float mz = s_m[h];
+        float lsum = 0.f;
+        for (int j0 = i0; j0 < n * kAttnPage; j0 += 16 * 8) {
+            float e[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int jj = j0 + 16 * u;
+                e[u] = jj < n * kAttnPage && p0 * kAttnPage + jj < L && h < G ? to_float(own[h * wl + jj]) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int jj = j0 + 16 * u;
+                if (jj < n * kAttnPage && p0 * kAttnPage + jj < L && h < G) lsum += expf(e[u] * scale - mz);
+            }
+        }
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+        if (i0 == 0) {
+            mpart[(rh * nz + z) * 16 + h] = mz;
+            mpart[(rh * nz + z) * 16 + 8 + h] = lsum;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    tl.phase(0);  // scores and pair of this split
+    // ---- every split's pair: wait until all have published, then M and 1 / sum in split order
+    if (tid == 0) {
+        atomicAdd(counter_a + rh, 1);
+        ok_s = 1;
+        const uint64_t t0 = globaltimer_ns();
+        while (*(volatile int *)(counter_a + rh) < nz) {
+            if (globaltimer_ns() - t0 > limit_ns) {
+                atomicCAS(err, 0, 6);
+                ok_s = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    if (tid < 8) {
+        float M = -INFINITY;
+        for (int zz = 0; zz < nz; ++zz) M = fmaxf(M, __ldcg(mpart + (rh * nz + zz) * 16 + tid));
+        float sum = 0.f;
+        for (int zz = 0; zz < nz; ++zz) {
+            const float l = __ldcg(mpart + (rh * nz + zz) * 16 + 8 + tid);
+            if (l > 0.f) sum += l * expf(__ldcg(mpart + (rh * nz + zz) * 16 + tid) - M);
+        }
+        minv[2 * tid] = M;
+        minv[2 * tid + 1] = 1.0f / sum;
+    }
+    __syncthreads();
+    tl.phase(1);  // normaliser
+    // ---- P of this split's keys: T(T(exp(s * scale - M)) * (1 / sum)), in place
+    {
+        const int h = tid >> 4, i0 = tid & 15;
+        const float M = minv[2 * h], inv = minv[2 * h + 1];
+        for (int jj = i0; jj < n * kAttnPage; jj += 16) {
+            const int j = p0 * kAttnPage + jj;
+            float pv = 0.f;
+            if (j < L && h < G)
+                pv = to_float(from_float<T>(to_float(from_float<T>(expf(to_float(own[h * wl + jj]) * scale - M))) * inv));
+            own[h * wl + jj] = from_float<T>(pv);
+        }
+    }
+    __syncthreads();
+    // ---- P . V over this split's V pages
+    constexpr int kDT = D / 16;
+    constexpr int kNA = kDT > 4 ? 2 : 1;
+    float o[kNA][4];
+#pragma unroll
+    for (int a = 0; a < kNA; ++a) o[a][0] = o[a][1] = o[a][2] = o[a][3] = 0.f;
+    ok = ok && ok_s;
+    for (int i = 0; i < n; ++i, ++consumed) {
+        const int slot = consumed % kAttnSlots;
+        if (!mbar_wait_bounded(bars + slot, (consumed / kAttnSlots) & 1, err, 5)) ok = false;
+        if (p0 + i == npages - 1 && L % kAttnPage) {
+            // rows past the sequence end hold stale cache bytes; their P is 0, but 0 * NaN is NaN
+            T *vw = reinterpret_cast<T *>(ring + slot * kPageBytes);
+            const int r0 = L - (p0 + i) * kAttnPage;
+            for (int e = tid; e < (kAttnPage - r0) * D; e += 128) vw[r0 * D + e] = from_float<T>(0.f);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+        }
+        const T *vt = reinterpret_cast<const T *>(ring + slot * kPageBytes);
+        if (ok) {
+#pragma unroll
+            for (int ks = 0; ks < kAttnPage / 16; ++ks) {
+                const int key0 = i * kAttnPage + ks * 16;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(own + g * wl + key0 + 2 * t);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(own + g * wl + key0 + 2 * t + 8);
+#pragma unroll
+                for (int a = 0; a < kNA; ++a) {
+                    const int d0 = (warp + 4 * a) * 16;
+                    const int mi = lane >> 3, r = lane & 7;
+                    const T *addr = vt + (ks * 16 + r + (mi >> 1) * 8) * D + d0 + (mi & 1) * 8;
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(smem_u32(addr), a0, a1, a2, a3);
+                    mma16<T>(o[a], a0, a1, a2, a3, b0, b1);
+                }
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && issued < 2 * n) {
+            const int sl = issued % kAttnSlots;
+            mbar_expect_tx(bars + sl, kPageBytes);
+            bulk_g2s(ring + sl * kPageBytes, page_src(issued), kPageBytes, bars + sl);
+            ++issued;
+        }
+    }
+    float *op = opart + (rh * nz + z) * 8 * D;
+#pragma unroll
+    for (int a = 0; a < kNA; ++a) {
+        const int d0 = (warp + 4 * a) * 16;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int d = d0 + g + (i >> 1) * 8, hh = 2 * t + (i & 1);
+            op[hh * D + d] = o[a][i];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    tl.phase(2);  // partial of this split
+    if (tid == 0) last = atomicAdd(counter + rh, 1) == nz - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    T *orow = out + (long)row * out_rs + (long)kvh * G * D;
+    for (int i4 = tid; i4 < G * D / 4; i4 += 128) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int z0 = 0; z0 < nz; z0 += 16) {
+            float4 v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                v[u] = z0 + u < nz ? __ldcg(reinterpret_cast<const float4 *>(opart + (rh * nz + z0 + u) * 8 * D) + i4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                if (z0 + u < nz) {
+                    acc.x += v[u].x;
+                    acc.y += v[u].y;
+                    acc.z += v[u].z;
+                    acc.w += v[u].w;
+                }
+        }
+        orow[4 * i4] = from_float<T>(acc.x);
+        orow[4 * i4 + 1] = from_float<T>(acc.y);
+        orow[4 * i4 + 2] = from_float<T>(acc.z);
+        orow[4 * i4 + 3] = from_float<T>(acc.w);
+    }
+    // every split has passed both waits: the counters start from zero next launch
+    if (tid == 0) {
+        counter[rh] = 0;
+        counter_a[rh] = 0;
+    }
+    tl.phase(3);  // combined
+}
+
+// Returns the launches made (0: not split; the caller launches one CTA per (row, kv head)).
+template <typename T, int D>
+int launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
                   int nrows, int max_len, const KVPaged &kv, int G, cudaStream_t s, bool pdl, bool early,
                   const AttnSplitWs &ws) {
     const char *env = getenv("WUKONG_SPLIT_ATTN");  // 0: one CTA per (row, kv head) always
-    if (env && env[0] == '0') return false;
+    if (env && env[0] == '0') return 0;
     const int pages = (max_len + kAttnPage - 1) / kAttnPage;
     const int units = nrows * kv.kv_heads;
     int nz = (2 * g_rt.num_sms + units - 1) / units;
@@ -819,15 +1103,47 @@ bool launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_
     if (nz > ws.max_splits) nz = ws.max_splits;
     // below 8 pages the second launch costs more than the split saves
     if (pages < 8 || nz < 2 || nrows > ws.max_rows || pages * kAttnPage > ws.lpad || kv.kv_heads > ws.max_kv_heads)
-        return false;
+        return 0;
     const int pps = (pages + nz - 1) / nz;
     nz = (pages + pps - 1) / pps;
-    if (nz < 2) return false;
+    if (nz < 2) return 0;
     const float scale = 1.0f / sqrtf((float)D);
+    {
+        // one launch when every split CTA fits on the GPU at once (they wait for each other)
+        const char *one = getenv("WUKONG_SPLIT_ATTN_FUSED");
+        const size_t smem_f = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 48 * 4 + 8 * D * 2 +
+                              (size_t)8 * pps * kAttnPage * 2;
+        auto kf = attn_split_fused_kernel<T, D>;
+        static int conf_f = 0;
+        if (!(one && one[0] == '0') && (int)smem_f <= g_rt.max_smem_optin) {
+            if ((int)smem_f > conf_f) {
+                WK_CHECK(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_f));
+                conf_f = (int)smem_f;
+            }
+            int per_sm = 0;
+            WK_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kf, 128, smem_f));
+            if ((long)kv.kv_heads * nrows * nz <= (long)per_sm * g_rt.num_sms) {
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3(kv.kv_heads, nrows, nz);
+                cfg.blockDim = dim3(128);
+                cfg.stream = s;
+                cfg.dynamicSmemBytes = smem_f;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+                attr[0].val.programmaticStreamSerializationAllowed = 1;
+                cfg.attrs = attr;
+                cfg.numAttrs = (pdl && g_rt.pdl) ? 1 : 0;
+                WK_CHECK(cudaLaunchKernelEx(&cfg, kf, out, out_rs, q, q_rs, seq_of_row, pos_of_row, kv, G, pps, scale,
+                                            ws.mpart, ws.opart, ws.counter, ws.counter_a, g_rt.d_error,
+                                            early ? 1 : 0, g_rt.wait_limit_ns));
+                return 1;
+            }
+        }
+    }
     const size_t smem_a = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + 32 * 4 + 8 * D * 2 +
                           (size_t)8 * pps * kAttnPage * 2;
     const size_t smem_b = (size_t)kAttnSlots * kAttnPage * D * 2 + kAttnSlots * 8 + (size_t)8 * pps * kAttnPage * 2;
-    if ((int)smem_a > g_rt.max_smem_optin || (int)smem_b > g_rt.max_smem_optin) return false;
+    if ((int)smem_a > g_rt.max_smem_optin || (int)smem_b > g_rt.max_smem_optin) return 0;
     auto ka = attn_split_scores_kernel<T, D>;
     auto kb = attn_split_pv_kernel<T, D>;
     static int conf_a = 0, conf_b = 0;
@@ -856,7 +1172,7 @@ bool launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_
     WK_CHECK(cudaLaunchKernelEx(&cfg, kb, out, out_rs, seq_of_row, pos_of_row, kv, G, pps, ws.lpad, scale,
                                 (const T *)ws.scores, (const float *)ws.minv, ws.opart, ws.counter, g_rt.d_error,
                                 early ? 1 : 0));
-    return true;
+    return 2;
 }
 
 template <typename T, int D>
@@ -1164,11 +1480,12 @@ int attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_o
     if constexpr (sizeof(T) == 2) {
         if (c.page == kAttnPage && G <= 8 && (c.hd == 64 || c.hd == 128) && ((uintptr_t)c.k % 16) == 0 &&
             ((uintptr_t)c.v % 16) == 0) {
-            if (ws && (c.hd == 64 ? launch_split<T, 64>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows, max_len,
-                                                        kv, G, s, pdl, early, *ws)
-                                  : launch_split<T, 128>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows,
-                                                         max_len, kv, G, s, pdl, early, *ws)))
-                return 2;
+            const int ns = !ws ? 0
+                           : c.hd == 64 ? launch_split<T, 64>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows,
+                                                              max_len, kv, G, s, pdl, early, *ws)
+                                        : launch_split<T, 128>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows,
+                                                               max_len, kv, G, s, pdl, early, *ws);
+            if (ns) return ns;
             if (c.hd == 64)
                 launch_decode_tc<T, 64>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows, max_len, kv, G, s, pdl,
                                         pf, pf_bytes, early);
