@@ -26,9 +26,9 @@ typedef struct wk_model wk_model;
 typedef struct {
     int n_layers, d_model, n_heads, n_kv_heads, head_dim, ffn, vocab;
     float eps;
-    int wtype;       /* dtype of the linear layers (GGML id: 1 F16, 8 Q8_0, 30 BF16) */
+    int wtype;       /* dtype of the linear layers (GGML id: 1 F16, 2 Q4_0, 8 Q8_0, 30 BF16) */
     int out_wtype;   /* dtype of output.weight */
-    int embd_wtype;  /* dtype of token_embd.weight (0 F32, 1 F16, 8 Q8_0, 30 BF16) */
+    int embd_wtype;  /* dtype of token_embd.weight (0 F32, 1 F16, 2 Q4_0, 8 Q8_0, 30 BF16) */
 } wk_config;
 
 const char *wk_last_error(void);
@@ -67,9 +67,28 @@ int wk_model_position(const wk_model *m);
  * the caller sets them.  Used to discard speculative or timed continuations. */
 int wk_model_truncate(wk_model *m, int n);
 
+/* Sampling instead of greedy argmax (the reference's predict is greedy and
+ * leaves sampling as a TODO, cuda.cu:988): temperature > 0 turns it on for
+ * the model's prefill and decode steps, temperature <= 0 back to greedy.  The
+ * candidates are the min(top_k, 256) largest logits (top_k <= 0: 256), equal
+ * values ordered by smaller index; top_p in (0, 1) keeps the shortest prefix
+ * of them whose probability reaches top_p.  The draw of the token at
+ * position p + 1 of sequence b uses the counter-based uniform of (seed, p, b),
+ * so a run is reproducible.  Call after wk_model_alloc_cache; not with
+ * tensor parallelism.  Returns 0 or -1. */
+int wk_model_set_sampling(wk_model *m, float temperature, int top_k, float top_p, unsigned long long seed);
+/* The same sampling over logits rows already on the device ([rows, vocab] of
+ * dtype F16, BF16 or F32, e.g. from cuda_classify), every row with RNG step
+ * `step`: device int32 tokens[rows]. */
+int wk_sample_logits(int *tokens, const void *logits, int rows, int vocab, int dtype, float temperature, int top_k,
+                     float top_p, unsigned long long seed, long long step);
+
 /* Synthetic weights, bit-identical to the CPU oracle's generator:
  * Irwin-Hall(4) normal(0, stdv) samples of a counter-based hash. */
 int wk_fill_random_q8_0(void *dst, long rows, int cols, uint64_t seed, float stdv);
+/* The same samples quantised to GGUF Q4_0 (d = largest-magnitude value / -8,
+ * nibble = min(15, (int)(x / d + 8.5))). */
+int wk_fill_random_q4_0(void *dst, long rows, int cols, uint64_t seed, float stdv);
 int wk_fill_random_f16(void *dst, long n, uint64_t seed, float stdv);
 int wk_fill_const_f32(void *dst, long n, float value);
 

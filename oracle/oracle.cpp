@@ -99,6 +99,23 @@ void decode_row(const void *w, int wtype, long row, int K, float *dst, int q8_ro
         }
         break;
     }
+    case ORC_Q4_0: {
+        /* GGUF Q4_0, dequantised by the reference's Q8_0 rule (cuda.cu:1104-1108):
+         * w = (half)(float(d) * (nibble - 8)); byte i holds values i and i + 16 */
+        const uint8_t *p = (const uint8_t *)w + row * (long)(K / 32) * 18;
+        for (int b = 0; b < K / 32; ++b) {
+            uint16_t s;
+            memcpy(&s, p + 18 * b, 2);
+            const float d = h2f(s);
+            for (int i = 0; i < 16; ++i) {
+                const uint8_t q = p[18 * b + 2 + i];
+                const float v0 = d * (float)((int)(q & 15) - 8), v1 = d * (float)((int)(q >> 4) - 8);
+                dst[32 * b + i] = q8_round_half ? f16_round(v0) : v0;
+                dst[32 * b + 16 + i] = q8_round_half ? f16_round(v1) : v1;
+            }
+        }
+        break;
+    }
     default:
         abort();
     }
@@ -151,6 +168,27 @@ void quantize_block(const float *x, uint8_t *dst) {
     }
 }
 
+/* ggml's Q4_0 quantisation (quantize_row_q4_0_reference, the published rule):
+ * d = (value of largest magnitude, first occurrence) / -8, nibble =
+ * min(15, (int)(x / d + 8.5)), byte i = nibble(x_i) | nibble(x_{i+16}) << 4. */
+void quantize_block_q4_0(const float *x, uint8_t *dst) {
+    float amax = 0.f, mx = 0.f;
+    for (int i = 0; i < 32; ++i)
+        if (fabsf(x[i]) > amax) {
+            amax = fabsf(x[i]);
+            mx = x[i];
+        }
+    const float d = mx / -8.0f;
+    const float id = d != 0.f ? 1.0f / d : 0.f;
+    uint16_t s = f2h_bits(d);
+    memcpy(dst, &s, 2);
+    for (int i = 0; i < 16; ++i) {
+        const int n0 = std::min(15, (int)(x[i] * id + 8.5f));
+        const int n1 = std::min(15, (int)(x[i + 16] * id + 8.5f));
+        dst[2 + i] = (uint8_t)(n0 | (n1 << 4));
+    }
+}
+
 }  // namespace
 
 extern "C" {
@@ -182,6 +220,28 @@ void orc_f32_to_bf16(const float *s, uint16_t *d, size_t n) {
 int orc_num_threads(void) { return omp_get_max_threads(); }
 void orc_set_f32_tf32(int on) { g_f32_tf32 = on; }
 void orc_set_threads(int n) { omp_set_num_threads(n); }
+
+void orc_gen_q4_0(uint8_t *out, int rows, int cols, uint64_t seed, float stdv) {
+    const float k = gen_k(stdv);
+#pragma omp parallel for schedule(static)
+    for (long r = 0; r < rows; ++r) {
+        float x[32];
+        for (int b = 0; b < cols / 32; ++b) {
+            const long blk = r * (cols / 32) + b;
+            for (int i = 0; i < 32; ++i) x[i] = gen_one(seed, (uint64_t)(blk * 32 + i), k);
+            quantize_block_q4_0(x, out + blk * 18);
+        }
+    }
+}
+
+void orc_quantize_q4_0(uint8_t *out, const float *x, int rows, int cols) {
+    for (long b = 0; b < (long)rows * cols / 32; ++b) quantize_block_q4_0(x + b * 32, out + b * 18);
+}
+
+void orc_dequant_q4_0(float *out, const uint8_t *blocks, int rows, int cols, int out_half) {
+#pragma omp parallel for schedule(static)
+    for (long r = 0; r < rows; ++r) decode_row(blocks, ORC_Q4_0, r, cols, out + r * cols, out_half);
+}
 
 /* cuda.cu:389-421: out = (T)((float)scale * q) -- the fp32 product is exact. */
 void orc_dequant_q8_0(float *out, const uint8_t *blocks, int rows, int cols, int out_half) {
@@ -384,6 +444,59 @@ void orc_argmax(int *out, const float *inp, int rows, int cols, int pack) {
                 }
             }
         out[r] = bidx;
+    }
+}
+
+/* Sampling beyond argmax.  The reference has none (cuda.cu:988 leaves it as a
+ * TODO), so this restates the library's published rule, not reference code:
+ * candidates = the min(top_k, 256) largest values (top_k <= 0: 256), ties by
+ * smaller index; e_i = exp((l_i - l_max) / temperature); prefix sums c_i; the
+ * shortest prefix m with c_m >= top_p * c_K (top_p outside (0, 1): all K);
+ * u = (top 24 bits of mix64(seed + 0x9E3779B97F4A7C15 * (step * 65536 + row + 1)))
+ * * 2^-24 * c_m; the token is the first candidate with c_i > u.  u_out (may be
+ * null) receives u / c_m and the relative distance of u to the nearest
+ * prefix-sum boundary, for tolerance checks. */
+void orc_sample(int *out, float *u_out, const float *logits, int rows, int V, float temperature, int top_k,
+                float top_p, uint64_t seed, const int64_t *steps) {
+    for (int r = 0; r < rows; ++r) {
+        const float *x = logits + (size_t)r * V;
+        const int K = std::min(top_k > 0 && top_k < 256 ? top_k : 256, V);
+        std::vector<int> idx(V);
+        for (int i = 0; i < V; ++i) idx[i] = i;
+        std::partial_sort(idx.begin(), idx.begin() + K, idx.end(),
+                          [&](int a, int b) { return x[a] > x[b] || (x[a] == x[b] && a < b); });
+        std::vector<float> c(K);
+        const float lmax = x[idx[0]], invt = 1.0f / temperature;
+        float run = 0.f;
+        for (int i = 0; i < K; ++i) {
+            run += expf((x[idx[i]] - lmax) * invt);
+            c[i] = run;
+        }
+        int m = K;
+        if (top_p > 0.f && top_p < 1.f) {
+            const float target = top_p * run;
+            for (int i = 0; i < K; ++i)
+                if (c[i] >= target) {
+                    m = i + 1;
+                    break;
+                }
+        }
+        const uint64_t h = mix64(seed + 0x9E3779B97F4A7C15ull * (uint64_t)(steps[r] * 65536 + r + 1));
+        const float frac = (float)(h >> 40) * (1.0f / 16777216.0f);
+        const float u = frac * c[m - 1];
+        int pick = m - 1;
+        for (int i = 0; i < m; ++i)
+            if (c[i] > u) {
+                pick = i;
+                break;
+            }
+        out[r] = idx[pick];
+        if (u_out) {
+            float dist = INFINITY;
+            for (int i = 0; i < m; ++i) dist = std::min(dist, fabsf(c[i] - u) / c[m - 1]);
+            u_out[2 * r] = frac;
+            u_out[2 * r + 1] = dist;
+        }
     }
 }
 

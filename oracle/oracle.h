@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q8_0 = 8, ORC_BF16 = 30 };
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_BF16 = 30 };
 
 /* element helpers */
 float orc_round(int act, float x);
@@ -54,6 +54,11 @@ void orc_gqa_sdpa(float *out, const float *qkv, int batch, int row, int NH, int 
 void orc_get_row(float *out, const float *inp, int batch, int row, int col, int idx);
 /* :480-531, with the kernel's exact tie order; pack = 16 / sizeof(T) */
 void orc_argmax(int *out, const float *inp, int rows, int cols, int pack);
+void orc_gen_q4_0(uint8_t *out, int rows, int cols, uint64_t seed, float stdv);
+void orc_quantize_q4_0(uint8_t *out, const float *x, int rows, int cols);
+void orc_dequant_q4_0(float *out, const uint8_t *blocks, int rows, int cols, int out_half);
+void orc_sample(int *out, float *u_out, const float *logits, int rows, int V, float temperature, int top_k,
+                float top_p, uint64_t seed, const int64_t *steps);
 /* :238-252 + :1232-1255; out in act grid (Q8_0 -> fp16) */
 void orc_embedding(float *out, const int *ids, const void *table, int n, int col, int dtype);
 

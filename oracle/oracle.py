@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_LIB_PATH = os.path.join(HERE, "_ref", "libwukong_ref.so")
 
-F32, F16, Q8_0, BF16 = 0, 1, 8, 30
+F32, F16, Q4_0, Q8_0, BF16 = 0, 1, 2, 8, 30
 
 
 def build():
@@ -44,6 +44,10 @@ def _load():
         "orc_gqa_sdpa": (None, [P, P, I, I, I, I, I, I]),
         "orc_get_row": (None, [P, P, I, I, I, I]),
         "orc_argmax": (None, [P, P, I, I, I]),
+        "orc_sample": (None, [P, P, P, I, I, F, I, F, ctypes.c_uint64, P]),
+        "orc_gen_q4_0": (None, [P, I, I, ctypes.c_uint64, F]),
+        "orc_quantize_q4_0": (None, [P, P, I, I]),
+        "orc_dequant_q4_0": (None, [P, P, I, I, I]),
         "orc_embedding": (None, [P, P, P, I, I, I]),
         "orc_gqa_layer": (None, [P, P, P, P, P, I, I, I, I, I, I, F, I, I, P, P, I]),
         "orc_ffn_layer": (None, [P, P, P, P, I, I, I, I, F, I, I]),
@@ -174,6 +178,19 @@ def argmax(x, rows, cols, pack):
     return out
 
 
+def sample(logits, temperature, top_k, top_p, seed, steps):
+    """Tokens drawn per row (the library's sampling rule, restated); also
+    returns per row (u / c_m, distance of u to the nearest prefix-sum boundary
+    relative to c_m)."""
+    x = _f32(logits)
+    rows, V = x.shape
+    out = np.empty(rows, np.int32)
+    u = np.empty((rows, 2), np.float32)
+    st = np.ascontiguousarray(np.broadcast_to(np.asarray(steps, np.int64), (rows,)))
+    lib().orc_sample(_p(out), _p(u), _p(x), rows, V, temperature, top_k, top_p, seed, _p(st))
+    return out, u
+
+
 def embedding(ids, table, col, dtype):
     ids = np.ascontiguousarray(ids, np.int32)
     out = np.empty((ids.size, col), np.float32)
@@ -184,6 +201,24 @@ def embedding(ids, table, col, dtype):
 def gen_q8_0(rows, cols, seed, std=0.02):
     out = np.empty(rows * cols // 32 * 34, np.uint8)
     lib().orc_gen_q8_0(_p(out), rows, cols, seed, std)
+    return out
+
+
+def gen_q4_0(rows, cols, seed, std=0.02):
+    out = np.empty(rows * cols // 32 * 18, np.uint8)
+    lib().orc_gen_q4_0(_p(out), rows, cols, seed, std)
+    return out
+
+
+def quantize_q4_0(x, rows, cols):
+    out = np.empty(rows * cols // 32 * 18, np.uint8)
+    lib().orc_quantize_q4_0(_p(out), _p(_f32(x)), rows, cols)
+    return out
+
+
+def dequant_q4_0(blocks, rows, cols, out_half=False):
+    out = np.empty((rows, cols), np.float32)
+    lib().orc_dequant_q4_0(_p(out), _p(np.ascontiguousarray(blocks, np.uint8)), rows, cols, int(out_half))
     return out
 
 

@@ -20,6 +20,8 @@ def make_weights(cfg, wtype, out_type, embd_type, seed, ctx):
     def W(rows, cols, s, wt=wtype, std=0.02):
         if wt == wk.Q8_0:
             return orc.gen_q8_0(rows, cols, s, std)
+        if wt == wk.Q4_0:
+            return orc.gen_q4_0(rows, cols, s, std)
         return orc.gen_f16(rows * cols, s, std)
 
     layers = []

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libwukong.so")
 ROOT = os.path.dirname(HERE)
 
-F32, F16, Q8_0, BF16, I32 = 0, 1, 8, 30, 26
+F32, F16, Q4_0, Q8_0, BF16, I32 = 0, 1, 2, 8, 30, 26
 
 _P, _I, _F, _S = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
 _U64, _L = ctypes.c_uint64, ctypes.c_long
@@ -66,7 +66,10 @@ EXT = {
     "wk_model_step_launches": (_I, [_P]),
     "wk_model_position": (_I, [_P]),
     "wk_model_truncate": (_I, [_P, _I]),
+    "wk_model_set_sampling": (_I, [_P, _F, _I, _F, _U64]),
+    "wk_sample_logits": (_I, [_P, _P, _I, _I, _I, _F, _I, _F, _U64, ctypes.c_longlong]),
     "wk_fill_random_q8_0": (_I, [_P, _L, _I, _U64, _F]),
+    "wk_fill_random_q4_0": (_I, [_P, _L, _I, _U64, _F]),
     "wk_fill_random_f16": (_I, [_P, _L, _U64, _F]),
     "wk_fill_const_f32": (_I, [_P, _L, _F]),
     "wk_gemv": (_I, [_P, _P, _P, _I, _I, _I, _I]),

@@ -21,6 +21,7 @@ namespace wk {
 enum DType : int {
     kF32 = 0,
     kF16 = 1,
+    kQ4_0 = 2,
     kQ8_0 = 8,
     kBF16 = 30,
     kDTypeCount = 36,
@@ -36,6 +37,14 @@ extern const DTypeInfo kDTypes[kDTypeCount];
 // Q8_0 block: fp16 scale followed by 32 int8 quants, 34 bytes, no padding.
 constexpr int kQ8Block = 32;
 constexpr int kQ8Bytes = 34;
+// GGUF Q4_0 block: fp16 scale d, then 16 bytes; byte i holds value i (low
+// nibble) and value i + 16 (high nibble), each stored as q + 8 (q in [-8, 7]).
+constexpr int kQ4Bytes = 18;
+// Row bytes of a [rows, K] weight of a GGUF dtype this library streams.
+__host__ __device__ inline long quant_row_bytes(int wtype, int K) {
+    return wtype == kQ8_0 ? (long)(K / 32) * kQ8Bytes : wtype == kQ4_0 ? (long)(K / 32) * kQ4Bytes
+                                                                       : (long)K * (wtype == kF32 ? 4 : 2);
+}
 
 // Activation element type that the reference instantiates for a weight dtype:
 // float for F32, bf16 for BF16, half for F16 and every quantised type
@@ -261,6 +270,15 @@ __device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, __half2 &lo, __half2 &h
     hi = __hsub2(*reinterpret_cast<__half2 *>(&h), bias);
 }
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
+// Four 4-bit fields (one per byte of n, each 0..15, the stored q + 8) -> two
+// half2 {q0,q1},{q2,q3}, exact: 1024 + n as the mantissa, minus 1032.
+__device__ __forceinline__ void u4x4_to_h2x2(uint32_t n, __half2 &lo, __half2 &hi) {
+    uint32_t l = __byte_perm(n, 0x64646464u, 0x5140);
+    uint32_t h = __byte_perm(n, 0x64646464u, 0x5342);
+    const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6408));  // 1032.0
+    lo = __hsub2(*reinterpret_cast<__half2 *>(&l), bias);
+    hi = __hsub2(*reinterpret_cast<__half2 *>(&h), bias);
+}
 
 // Argmax order of the reference's argmax kernel (cuda.cu:480-531) as a sort key:
 // element idx of a row is read by thread (idx / pack) % 256 in iteration
@@ -309,6 +327,38 @@ __device__ __forceinline__ void q8_block(const uint8_t *r0, const uint8_t *r1, i
         __half2 lo0, hi0, lo1, hi1;
         i8x4_to_h2x2(q0[h], lo0, hi0);
         i8x4_to_h2x2(q1[h], lo1, hi1);
+        const uint32_t a0 = h2_as_u32(__hmul2(lo0, s0)), a2 = h2_as_u32(__hmul2(hi0, s0));
+        const uint32_t a1 = h2_as_u32(__hmul2(lo1, s1)), a3 = h2_as_u32(__hmul2(hi1, s1));
+        const uint2 xv = h ? x1 : x0;
+        mma_f16(c[h], a0, a1, a2, a3, xv.x, xv.y);
+    }
+}
+
+// One Q4_0 block (32 k, two MMA k-slices) of rows g and g + 8 of the staged
+// tile: lane t takes quant bytes 4t..4t+3 (values 4t..4t+3 of the first
+// 16-slice in their low nibbles, of the second in their high nibbles).  Odd
+// blocks start their quants 4-byte aligned (18 * odd + 2 = 0 mod 4).
+__device__ __forceinline__ void q4_block(const uint8_t *r0, const uint8_t *r1, int off, bool odd, int t, uint2 x0,
+                                         uint2 x1, float (&c)[2][4]) {
+    const __half2 s0 = __half2half2(*reinterpret_cast<const __half *>(r0 + off));
+    const __half2 s1 = __half2half2(*reinterpret_cast<const __half *>(r1 + off));
+    uint32_t w0, w1;
+    if (odd) {
+        w0 = *reinterpret_cast<const uint32_t *>(r0 + off + 2 + 4 * t);
+        w1 = *reinterpret_cast<const uint32_t *>(r1 + off + 2 + 4 * t);
+    } else {
+        const uint32_t *p0 = reinterpret_cast<const uint32_t *>(r0 + off + 4 * t);
+        const uint32_t *p1 = reinterpret_cast<const uint32_t *>(r1 + off + 4 * t);
+        w0 = __byte_perm(p0[0], p0[1], 0x5432);
+        w1 = __byte_perm(p1[0], p1[1], 0x5432);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t n0 = h ? (w0 >> 4) & 0x0F0F0F0Fu : w0 & 0x0F0F0F0Fu;
+        const uint32_t n1 = h ? (w1 >> 4) & 0x0F0F0F0Fu : w1 & 0x0F0F0F0Fu;
+        __half2 lo0, hi0, lo1, hi1;
+        u4x4_to_h2x2(n0, lo0, hi0);
+        u4x4_to_h2x2(n1, lo1, hi1);
         const uint32_t a0 = h2_as_u32(__hmul2(lo0, s0)), a2 = h2_as_u32(__hmul2(hi0, s0));
         const uint32_t a1 = h2_as_u32(__hmul2(lo1, s1)), a3 = h2_as_u32(__hmul2(hi1, s1));
         const uint2 xv = h ? x1 : x0;

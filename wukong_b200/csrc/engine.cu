@@ -100,6 +100,35 @@ __global__ void fill_q8_0_kernel(uint8_t *dst, long nblk, uint64_t seed, float k
     }
 }
 
+// GGUF Q4_0 quantisation of the same normal samples (the published ggml
+// rule): d = (value of largest magnitude) / -8, n = min(15, (int)(x / d + 8.5)).
+__global__ void fill_q4_0_kernel(uint8_t *dst, long nblk, uint64_t seed, float k) {
+    long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblk) return;
+    float x[32];
+    float amax = 0.f, mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        x[i] = gen_one(seed, (uint64_t)(b * 32 + i), k);
+        if (fabsf(x[i]) > amax) {
+            amax = fabsf(x[i]);
+            mx = x[i];
+        }
+    }
+    const float d = mx / -8.0f;
+    const float id = d != 0.f ? 1.0f / d : 0.f;
+    const unsigned short bits = __half_as_ushort(__float2half_rn(d));
+    uint8_t *o = dst + b * kQ4Bytes;
+    o[0] = (uint8_t)(bits & 0xff);
+    o[1] = (uint8_t)(bits >> 8);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int n0 = min(15, (int)(x[i] * id + 8.5f));
+        const int n1 = min(15, (int)(x[i + 16] * id + 8.5f));
+        o[2 + i] = (uint8_t)(n0 | (n1 << 4));
+    }
+}
+
 __global__ void fill_f16_kernel(__half *dst, long n, uint64_t seed, float k) {
     long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) dst[i] = __float2half_rn(gen_one(seed, (uint64_t)i, k));
@@ -141,6 +170,12 @@ __global__ void embed_kernel(T *__restrict__ out, const int *__restrict__ ids, c
             const uint8_t *blk = table + (id * (col / 32) + i / 32) * 34;
             const float s = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
             v = __half2float(__float2half_rn(s * (float)(int8_t)blk[2 + (i & 31)]));
+        } else if (dtype == kQ4_0) {
+            const uint8_t *blk = table + (id * (col / 32) + i / 32) * kQ4Bytes;
+            const float s = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+            const int j = i & 31;
+            const int nib = j < 16 ? (blk[2 + j] & 15) : (blk[2 + j - 16] >> 4);
+            v = __half2float(__float2half_rn(s * (float)(nib - 8)));
         } else if (dtype == kF16) {
             v = __half2float(reinterpret_cast<const __half *>(table)[id * col + i]);
         } else if (dtype == kBF16) {
@@ -198,6 +233,10 @@ struct wk_model {
     unsigned long long mk_base = 0;
     int mk_stages = 0;
     size_t mk_smem = 0;
+    // sampling instead of the fused argmax (wk_model_set_sampling)
+    int sampling = 0;
+    SampleArgs sample;
+    void *logits = nullptr;  // [max_batch, vocab] logits of the last rows
 };
 
 namespace {
@@ -256,9 +295,7 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
     // (qkv -> o, o -> fc, fc -> down, down -> next qkv); the last down
     // prefetches the head of the logits matrix.  Attention prefetches nothing
     // (its few CTAs would queue the prefetches ahead of their own page loads).
-    auto wbytes = [&](long rows, int K, int wt) -> long {
-        return wt == kQ8_0 ? rows * (K / 32) * 34 : rows * (long)K * 2;
-    };
+    auto wbytes = [&](long rows, int K, int wt) -> long { return rows * quant_row_bytes(wt, K); };
     // At most kL2PrefetchMax bytes ahead: a larger prefetch queues ahead of the
     // next kernel's own activation loads in the memory system (measured, 8B:
     // 58 MB ahead of up|gate delayed its prologue by ~5 us; 12 MB: 2.79 -> 2.67
@@ -454,8 +491,21 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
             }
         } else {
             a.tokens = tokens + b0;
+            if (m->sampling) {
+                a.out = (char *)m->logits + (size_t)b0 * c.vocab * es;
+                a.ldo = c.vocab;
+            }
         }
         gemv(a, m->act, s);
+    }
+    if (m->sampling && !m->tp) {
+        // the draw replaces the argmax; RNG step = the position of each sequence's last row
+        SampleArgs sp = m->sample;
+        sp.pos = pos;
+        sp.pos_stride = last_row_stride;
+        sp.pos_off = last_row_stride - 1;
+        sample_rows(tokens, m->logits, c.vocab, batch, c.vocab, m->act, sp, s);
+        ++launches;
     }
     if (m->tp && m->link.world == 1) {
         tp_argmax_combine(tokens, m->win_send, m->win_recv, batch, 16 / (int)es, s);
@@ -626,7 +676,7 @@ void wk_model_destroy(wk_model *m) {
                     m->x, m->q, m->att, m->h, m->xn, m->part_val, m->part_key, m->counter,
                     m->p32, m->win_send, m->win_recv, m->d_mk_layers, m->d_mk_maps, m->d_mk_bar,
                     m->attn_ws.scores, m->attn_ws.mpart, m->attn_ws.opart, m->attn_ws.counter,
-                    m->attn_ws.minv};
+                    m->attn_ws.minv, m->logits};
     for (void *p : bufs)
         if (p) cudaFree(p);
     free(m->layers);
@@ -700,6 +750,28 @@ int wk_model_alloc_cache(wk_model *m, int max_batch, int max_ctx) {
     return 0;
 }
 
+int wk_model_set_sampling(wk_model *m, float temperature, int top_k, float top_p, unsigned long long seed) {
+    if (!m) return fail("null model");
+    if (m->tp && temperature > 0.f) return fail("sampling is not available with tensor parallelism");
+    if (!m->kpool) return fail("wk_model_set_sampling must come after wk_model_alloc_cache");
+    set_device_current();
+    if (temperature > 0.f && !m->logits)
+        WK_TRY(cudaMallocAsync(&m->logits, (size_t)m->max_batch * m->cfg.vocab * act_size(m->act), stream()));
+    m->sampling = temperature > 0.f ? 1 : 0;
+    m->sample = SampleArgs();
+    m->sample.temperature = temperature > 0.f ? temperature : 1.f;
+    m->sample.top_k = top_k;
+    m->sample.top_p = top_p;
+    m->sample.seed = seed;
+    // the decode graph holds the previous choice
+    if (m->graph) {
+        WK_TRY(cudaStreamSynchronize(stream()));
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    return 0;
+}
+
 int wk_model_set_tp(wk_model *m, int enable) {
     if (!m) return fail("null model");
     if (m->kpool) return fail("wk_model_set_tp must come before wk_model_alloc_cache");
@@ -753,7 +825,7 @@ int wk_model_decode_step(wk_model *m) {
     cudaStream_t s = stream();
     const int B = m->batch;
     if (m->mk_mode < 0) mk_setup(m);
-    if (m->mk_mode == 1 && B <= 8) {
+    if (m->mk_mode == 1 && B <= 8 && !m->sampling) {
         if (ensure_rows(m, 8 * B)) return -1;
         MkArgs a = m->mk;
         a.B = B;
@@ -823,6 +895,16 @@ int wk_fill_random_q8_0(void *dst, long rows, int cols, uint64_t seed, float std
     const long nblk = rows * (cols / 32);
     const float k = stdv / 37837.227f;
     fill_q8_0_kernel<<<(unsigned)((nblk + 255) / 256), 256, 0, stream()>>>((uint8_t *)dst, nblk, seed, k);
+    WK_TRY(cudaGetLastError());
+    return 0;
+}
+
+int wk_fill_random_q4_0(void *dst, long rows, int cols, uint64_t seed, float stdv) {
+    if (cols % 32) return fail("cols must be a multiple of 32");
+    ensure_init();
+    const long nblk = rows * (cols / 32);
+    fill_q4_0_kernel<<<(unsigned)((nblk + 255) / 256), 256, 0, stream()>>>((uint8_t *)dst, nblk, seed,
+                                                                          stdv / 37837.227f);
     WK_TRY(cudaGetLastError());
     return 0;
 }

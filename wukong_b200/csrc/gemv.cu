@@ -46,6 +46,12 @@ template <> struct WFmt<kQ8_0> {
     static __host__ __device__ long row_bytes(int K) { return (long)(K / 32) * 34; }
     static __host__ __device__ int chunk_bytes(int elems) { return elems / 32 * 34; }
 };
+template <> struct WFmt<kQ4_0> {
+    static constexpr int kChunk = 256;  // elements per row per stage
+    static constexpr int kRowB = 144;   // bytes per row per stage (8 blocks of 18)
+    static __host__ __device__ long row_bytes(int K) { return (long)(K / 32) * 18; }
+    static __host__ __device__ int chunk_bytes(int elems) { return elems / 32 * 18; }
+};
 template <> struct WFmt<kF16> {
     static constexpr int kChunk = 128;
     static constexpr int kRowB = 256;
@@ -156,7 +162,25 @@ __device__ __forceinline__ void consume_unit(const GemvArgs &a, const Smem &sm, 
     const bool has_x = g < M;
     const uint2 *xl = sm.xsrc + (has_x ? g : 0) * sm.xld + (e0 / 16) * 4 + t;  // slice e0/16 of row g
     constexpr int xstep = 4;                                                   // uint2 per slice
-    if constexpr (WT == kQ8_0) {
+    if constexpr (WT == kQ4_0) {
+        const int nblk = elems / 32;
+        if (nblk == 8) {
+            uint2 xv[16];
+#pragma unroll
+            for (int s = 0; s < 16; ++s) {
+                xv[s] = xl[s * xstep];
+                if (!has_x) xv[s] = make_uint2(0u, 0u);
+            }
+#pragma unroll
+            for (int b = 0; b < 8; ++b) q4_block(r0, r1, b * 18, (b & 1) != 0, t, xv[2 * b], xv[2 * b + 1], c);
+        } else {
+            for (int b = 0; b < nblk; ++b) {
+                uint2 x0 = xl[(2 * b) * xstep], x1 = xl[(2 * b + 1) * xstep];
+                if (!has_x) x0 = x1 = make_uint2(0u, 0u);
+                q4_block(r0, r1, b * 18, (b & 1) != 0, t, x0, x1, c);
+            }
+        }
+    } else if constexpr (WT == kQ8_0) {
         const int nblk = elems / 32;
         if (nblk == 8) {
             // full chunk: fetch the 16 B fragments first so their latency overlaps
@@ -844,7 +868,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
 }
 
 size_t gemv_smem_bytes(int K, int M, int wt, bool norm, int ns = kStages) {
-    const int chunk = wt == kQ8_0 ? WFmt<kQ8_0>::kChunk : WFmt<kF16>::kChunk;
+    const int chunk = (wt == kQ8_0 || wt == kQ4_0) ? 256 : WFmt<kF16>::kChunk;
     const int Kpad = (K + chunk - 1) / chunk * chunk;
     const bool stage = norm || (size_t)M * Kpad * 2 <= kXStageMax;
     return (size_t)kWarps * ns * kStageBytes + kWarps * ns * 8 + (stage ? (size_t)Kpad * M * 2 : 0) +
@@ -876,7 +900,7 @@ template <typename T, int WT, int NS> void launch(const GemvArgs &a, int grid, s
 }  // namespace
 
 bool gemv_supported(int wtype, int act, int K) {
-    if (wtype == kQ8_0) return act == kF16 && K % 32 == 0;
+    if (wtype == kQ8_0 || wtype == kQ4_0) return act == kF16 && K % 32 == 0;
     if (wtype == kF16) return act == kF16 && K % 16 == 0;
     if (wtype == kBF16) return act == kBF16 && K % 16 == 0;
     return false;
@@ -887,11 +911,13 @@ void gemv(GemvArgs a, int act, cudaStream_t s) {
     if (a.epi == EPI_ARESID && (a.tp.world < 2 || !a.tp.peers || (a.N + kTileRows - 1) / kTileRows > kTpMaxTiles))
         WK_PANIC("gemv: the all-reduce epilogue needs the peer exchange and at most %d tiles", kTpMaxTiles);
     if (!gemv_supported(a.wtype, act, a.K)) WK_PANIC("gemv: unsupported wtype %d / act %d / K %d", a.wtype, act, a.K);
-    const long rb = a.wtype == kQ8_0 ? (long)(a.K / 32) * 34 : (long)a.K * 2;
+    const long rb = quant_row_bytes(a.wtype, a.K);
     // weight tiles stream by TMA when rows are 16-byte aligned
     const CUtensorMap *map = nullptr;
     if (((uintptr_t)a.w % 16 == 0) && (rb % 16 == 0)) {
-        const int box_inner = a.wtype == kQ8_0 ? WFmt<kQ8_0>::kRowB / 2 : WFmt<kF16>::kRowB / 2;
+        const int box_inner = a.wtype == kQ8_0   ? WFmt<kQ8_0>::kRowB / 2
+                              : a.wtype == kQ4_0 ? WFmt<kQ4_0>::kRowB / 2
+                                                 : WFmt<kF16>::kRowB / 2;
         const long rows = a.epi == EPI_SWIGLU ? 2L * a.F : (long)a.N;
         map = weight_map(a.w, rows, rb, box_inner, a.epi == EPI_SWIGLU ? 8 : kTileRows);
     }
@@ -944,6 +970,8 @@ void gemv(GemvArgs a, int act, cudaStream_t s) {
     if (ns == 2) {
         if (a.wtype == kQ8_0)
             launch<__half, kQ8_0, 2>(a, grid, smem_used, s, pdl);
+        else if (a.wtype == kQ4_0)
+            launch<__half, kQ4_0, 2>(a, grid, smem_used, s, pdl);
         else if (a.wtype == kF16)
             launch<__half, kF16, 2>(a, grid, smem_used, s, pdl);
         else
@@ -951,6 +979,8 @@ void gemv(GemvArgs a, int act, cudaStream_t s) {
     } else {
         if (a.wtype == kQ8_0)
             launch<__half, kQ8_0, kStages>(a, grid, smem_used, s, pdl);
+        else if (a.wtype == kQ4_0)
+            launch<__half, kQ4_0, kStages>(a, grid, smem_used, s, pdl);
         else if (a.wtype == kF16)
             launch<__half, kF16, kStages>(a, grid, smem_used, s, pdl);
         else

@@ -534,7 +534,8 @@ void prefix_cache_note_upload(void *dst, const void *src, size_t size) {
 void prefix_cache_embedding(void *out, const int *ids, const void *embd, int batch, int row, int col, int dtype) {
     const int out_act = dtype == kF32 ? kF32 : (dtype == kBF16 ? kBF16 : kF16);
     const DTypeInfo &info = kDTypes[dtype];
-    const size_t out_row_bytes = dtype == kQ8_0 ? (size_t)col * 2 : (size_t)col / info.block_size * info.type_size;
+    const size_t out_row_bytes = (dtype == kQ8_0 || dtype == kQ4_0) ? (size_t)col * 2
+                                                                     : (size_t)col / info.block_size * info.type_size;
     int P = 0;
     const int *hids = g_sess.enabled ? find_shadow(ids, sizeof(int) * (size_t)batch * row) : nullptr;
     if (hids) {

@@ -261,8 +261,9 @@ void cuda_matmul(void *out, const void *inp, const void *weight, const void *bia
                  int dtype) {
     ensure_init();
     if (dtype < 0 || dtype >= kDTypeCount) WK_PANIC("Unsupported quantization type: %d", dtype);
-    if (dtype != kF32 && dtype != kF16 && dtype != kBF16 && dtype != kQ8_0)
+    if (dtype != kF32 && dtype != kF16 && dtype != kBF16 && dtype != kQ8_0 && dtype != kQ4_0)
         WK_PANIC("Unsupported quantization type: %s", kDTypes[dtype].name);
+    if (dtype == kQ4_0 && column % 32) WK_PANIC("Q4_0 weights need K %% 32 == 0 (K=%d)", column);
     if (bias && ((uintptr_t)bias % 16)) WK_PANIC("bias must be aligned to 16 bytes");
     matmul(out, inp, weight, bias, row, column, oc, dtype, act_of(dtype), stream());
 }

@@ -45,6 +45,48 @@ template <typename T> void dequant_q8_0(T *out, const void *in, long nblocks, cu
 template void dequant_q8_0<float>(float *, const void *, long, cudaStream_t);
 template void dequant_q8_0<__half>(__half *, const void *, long, cudaStream_t);
 
+// ------------------------------------------------------------ Q4_0 dequantise
+// The reference dequantises only Q8_0 (cuda.cu:1006-1012) though its dtype table
+// lists Q4_0 (cuda.cu:5-42); this applies its Q8_0 rule to GGUF Q4_0 blocks:
+// out = (T)(float(d) * (n - 8)) for the stored nibble n (exact product).
+template <typename T>
+__global__ void __launch_bounds__(256) dequant_q4_0_kernel(T *__restrict__ out, const uint8_t *__restrict__ in,
+                                                           long nblocks) {
+    const long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    const uint8_t *blk = in + b * kQ4Bytes;
+    const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+    T *o = out + b * 32;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        o[i] = from_float<T>(d * (float)((int)(blk[2 + i] & 15) - 8));
+        o[i + 16] = from_float<T>(d * (float)((int)(blk[2 + i] >> 4) - 8));
+    }
+}
+
+template <typename T> void dequant_q4_0(T *out, const void *in, long nblocks, cudaStream_t s) {
+    if (nblocks <= 0) return;
+    dequant_q4_0_kernel<T><<<(unsigned)((nblocks + 255) / 256), 256, 0, s>>>(out, (const uint8_t *)in, nblocks);
+    WK_CHECK_LAUNCH();
+}
+template void dequant_q4_0<float>(float *, const void *, long, cudaStream_t);
+template void dequant_q4_0<__half>(__half *, const void *, long, cudaStream_t);
+
+template <typename T>
+__global__ void gather_q4_0_kernel(T *__restrict__ out, const int *__restrict__ ids, const uint8_t *__restrict__ table,
+                                   int n, int col) {
+    const int r = blockIdx.x;
+    if (r >= n) return;
+    const uint8_t *row = table + (size_t)ids[r] * (col / 32) * kQ4Bytes;
+    for (int i = threadIdx.x; i < col; i += blockDim.x) {
+        const uint8_t *blk = row + (i / 32) * kQ4Bytes;
+        const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+        const int j = i & 31;
+        const int nib = j < 16 ? (blk[2 + j] & 15) : (blk[2 + j - 16] >> 4);
+        out[(size_t)r * col + i] = from_float<T>(d * (float)(nib - 8));
+    }
+}
+
 // ------------------------------------------------------------ embedding
 // cuda.cu:238-252, :1232-1255: byte gather of whole rows for plain dtypes; for
 // Q8_0 the gathered blocks are dequantised to half (fused here).
@@ -83,6 +125,11 @@ void embedding(void *out, const int *ids, const void *table, int n, int col, int
             gather_q8_0_kernel<float><<<n, 256, 0, s>>>((float *)out, ids, (const uint8_t *)table, n, col);
         else
             gather_q8_0_kernel<__half><<<n, 256, 0, s>>>((__half *)out, ids, (const uint8_t *)table, n, col);
+    } else if (dtype == kQ4_0) {
+        if (out_act == kF32)
+            gather_q4_0_kernel<float><<<n, 256, 0, s>>>((float *)out, ids, (const uint8_t *)table, n, col);
+        else
+            gather_q4_0_kernel<__half><<<n, 256, 0, s>>>((__half *)out, ids, (const uint8_t *)table, n, col);
     } else {
         const DTypeInfo &info = kDTypes[dtype];
         size_t row_bytes = (size_t)col / info.block_size * info.type_size;
@@ -388,16 +435,19 @@ extern "C" {
 void cuda_dequantize(void *out, const void *inp, int row, int col, int type) {
     ensure_init();
     if (type < 0 || type >= kDTypeCount) WK_PANIC("Unsupported quantization type: %d", type);
-    if (type != kQ8_0) WK_PANIC("Unsupported quantization type: %s", kDTypes[type].name);
+    if (type != kQ8_0 && type != kQ4_0) WK_PANIC("Unsupported quantization type: %s", kDTypes[type].name);
     if (col % kQ8Block) WK_PANIC("column count %d is not a multiple of %d", col, kQ8Block);
-    dequant_q8_0<float>((float *)out, inp, (long)row * (col / kQ8Block), stream());
+    if (type == kQ4_0)
+        dequant_q4_0<float>((float *)out, inp, (long)row * (col / 32), stream());
+    else
+        dequant_q8_0<float>((float *)out, inp, (long)row * (col / kQ8Block), stream());
 }
 
 // cuda.cu:1232-1255
 void cuda_embedding(void *out, const void *inp, const void *embd, int batch, int row, int col, int dtype) {
     ensure_init();
     if (dtype < 0 || dtype >= kDTypeCount) WK_PANIC("Unsupported quantization type: %d", dtype);
-    if (dtype != kF32 && dtype != kF16 && dtype != kBF16 && dtype != kQ8_0)
+    if (dtype != kF32 && dtype != kF16 && dtype != kBF16 && dtype != kQ8_0 && dtype != kQ4_0)
         WK_PANIC("Unsupported embedding type: %s", kDTypes[dtype].name);
     if (col % kDTypes[dtype].block_size) WK_PANIC("column count %d is not a multiple of the block size", col);
     prefix_cache_embedding(out, (const int *)inp, embd, batch, row, col, dtype);

@@ -163,6 +163,22 @@ void gemm_tc(GemmArgs a, int act, cudaStream_t s);
 // (measured, 8192 x 2048 Q8_0, M = 16: 19.6 us on tcgen05, 24.3 us as two 8-row GEMV passes).
 constexpr int kTcMinRows = 16;
 
+// ---------------------------------------------------------------- sampling.cu
+// Temperature / top-k / top-p sampling of one token per logits row.  The RNG
+// step of row b is pos[b * pos_stride + pos_off] when pos is set, else step.
+struct SampleArgs {
+    float temperature = 1.f;
+    int top_k = 0;
+    float top_p = 1.f;
+    unsigned long long seed = 0;
+    long long step = 0;
+    const int *pos = nullptr;
+    long pos_stride = 1;
+    int pos_off = 0;
+};
+void sample_rows(int *tokens, const void *logits, long ld, int rows, int V, int act, const SampleArgs &p,
+                 cudaStream_t s);
+
 // ---------------------------------------------------------------- ops.cu
 template <typename T> void dequant_q8_0(T *out, const void *in, long nblocks, cudaStream_t s);
 void embedding(void *out, const int *ids, const void *table, int n, int col, int dtype, int out_act, cudaStream_t s);
