@@ -53,6 +53,21 @@ int wk_model_prefill(wk_model *m, const int *ids, int batch, int n, int *tokens_
  * appends one position, writes the next tokens to the internal token buffer.
  * The first call captures the step into a CUDA graph; later calls replay it. */
 int wk_model_decode_step(wk_model *m);
+/* Continuous batching (no counterpart in the reference, whose Go loop decodes
+ * one sequence at a time, llm/model.go:116-178): sequences of different
+ * lengths join and leave the decode batch while it runs.  Each lives in a
+ * slot 0..max_batch-1 of the paged cache.  wk_model_add_seqs prefills count
+ * new sequences (ids: device int32, the prompts back to back; lens: host int
+ * [count]) into the lowest free slots (host slots_out [count]), appends them as
+ * the last rows of the batch and writes their first generated tokens there.
+ * wk_model_remove_seq drops a slot's sequence (the last row takes its row).
+ * wk_model_rows writes the slot of every decode row (host int [batch]) and
+ * returns the batch size; wk_model_tokens / wk_model_next_ids are in row
+ * order.  A decode step advances every row by one position; the batch's
+ * graph is re-captured after the batch changes.  Not with tensor parallelism. */
+int wk_model_add_seqs(wk_model *m, const int *ids, const int *lens, int count, int *slots_out);
+int wk_model_remove_seq(wk_model *m, int slot);
+int wk_model_rows(const wk_model *m, int *slots);
 /* device int32 [batch]: tokens produced by the latest prefill / decode step */
 const int *wk_model_tokens(const wk_model *m);
 /* device int32 [batch]: input tokens of the next decode step (writable) */

@@ -66,6 +66,9 @@ EXT = {
     "wk_model_step_launches": (_I, [_P]),
     "wk_model_position": (_I, [_P]),
     "wk_model_truncate": (_I, [_P, _I]),
+    "wk_model_add_seqs": (_I, [_P, _P, _P, _I, _P]),
+    "wk_model_remove_seq": (_I, [_P, _I]),
+    "wk_model_rows": (_I, [_P, _P]),
     "wk_model_set_sampling": (_I, [_P, _F, _I, _F, _U64]),
     "wk_sample_logits": (_I, [_P, _P, _I, _I, _I, _F, _I, _F, _U64, ctypes.c_longlong]),
     "wk_fill_random_q8_0": (_I, [_P, _L, _I, _U64, _F]),

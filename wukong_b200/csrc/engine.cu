@@ -53,6 +53,14 @@ __global__ void advance_kernel(int *ids, const int *tokens, int *pos, int batch)
     }
 }
 
+// rows[r] of src -> row r of dst (rows of row_u4 16-byte words)
+__global__ void gather_rows_by_index_kernel(uint4 *__restrict__ dst, const uint4 *__restrict__ src,
+                                            const int *__restrict__ rows, int row_u4) {
+    const int r = blockIdx.x;
+    const long from = (long)rows[r] * row_u4;
+    for (int i = threadIdx.x; i < row_u4; i += blockDim.x) dst[(long)r * row_u4 + i] = src[from + i];
+}
+
 __global__ void iota_kernel(int *p, int n, int v0, int step) {
     int i = threadIdx.x + blockIdx.x * blockDim.x;
     if (i < n) p[i] = v0 + i * step;
@@ -233,6 +241,11 @@ struct wk_model {
     unsigned long long mk_base = 0;
     int mk_stages = 0;
     size_t mk_smem = 0;
+    // continuous batching: decode row r serves the sequence in slot row_slot[r]
+    // (d_seq on the device); slot_pos holds each slot's length on the host
+    int *row_slot = nullptr, *slot_pos = nullptr;
+    unsigned char *slot_used = nullptr;
+    int *d_meta = nullptr;  // staging of per-row metadata uploads [4 * rows_cap + 4 * max_batch]
     // sampling instead of the fused argmax (wk_model_set_sampling)
     int sampling = 0;
     SampleArgs sample;
@@ -278,8 +291,18 @@ int reduce_partials(wk_model *m, int rows, cudaStream_t s) {
 // attention length.  Returns the number of kernel launches.
 constexpr long kL2PrefetchMax = 12L << 20;
 
+// Prefill of sequences of different lengths (continuous batching): group i
+// holds activation rows [row0[i], row0[i] + len[i]) of the sequence in slot
+// slot[i], positions 0..len[i]-1; last_rows / last_pos (device) list each
+// group's last row and its position.
+struct PrefillGroups {
+    int count = 0;
+    const int *row0 = nullptr, *len = nullptr, *slot = nullptr;  // host
+    const int *last_rows = nullptr, *last_pos = nullptr;         // device
+};
+
 int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_len, int batch, int last_row_stride,
-               int *tokens) {
+               int *tokens, const PrefillGroups *pg = nullptr) {
     const wk_config &c = m->cfg;
     const size_t es = act_size(m->act);
     const int d = c.d_model, col = c.n_heads * c.head_dim;
@@ -353,7 +376,27 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
         }
         // prefill: batch sequences of last_row_stride positions from 0, flash-style
         int pf = -1;
-        if (rows > batch && rows == batch * last_row_stride) {
+        if (pg) {
+            // each new sequence over its own slot's pages
+            pf = 0;
+            for (int i = 0; i < pg->count && pf >= 0; ++i) {
+                PagedKV kg = kv;
+                kg.block_table = kv.block_table + (long)pg->slot[i] * kv.max_pages;
+                const size_t o = (size_t)pg->row0[i] * col * es;
+                const int r = m->act == kF16
+                                  ? attention_prefill_paged<__half>((__half *)((char *)m->att + o), col,
+                                                                    (const __half *)((const char *)m->q + o), col, 1,
+                                                                    pg->len[i], 0, kg, c.n_heads, s)
+                                  : attention_prefill_paged<__nv_bfloat16>(
+                                        (__nv_bfloat16 *)((char *)m->att + o), col,
+                                        (const __nv_bfloat16 *)((const char *)m->q + o), col, 1, pg->len[i], 0, kg,
+                                        c.n_heads, s);
+                pf = r < 0 ? -1 : pf + r;
+            }
+            // shapes the flash kernel does not take: the per-row kernel over all rows (after any
+            // launched groups, which it simply recomputes)
+            if (pf > 0) launches += pf;
+        } else if (rows > batch && rows == batch * last_row_stride) {
             if (m->act == kF16)
                 pf = attention_prefill_paged<__half>((__half *)m->att, col, (const __half *)m->q, col, batch,
                                                      last_row_stride, 0, kv, c.n_heads, s);
@@ -460,13 +503,23 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
         }
     }
     // logits + argmax on the last row of each sequence
+    const void *xlast = m->x;
+    if (pg) {
+        // the groups' last rows, gathered into one [batch, d] block
+        gather_rows_by_index_kernel<<<batch, 128, 0, s>>>((uint4 *)m->xn, (const uint4 *)m->x, pg->last_rows,
+                                                          (int)(d * es / 16));
+        WK_CHECK_LAUNCH();
+        ++launches;
+        xlast = m->xn;
+        last_row_stride = 1;
+    }
     for (int b0 = 0; b0 < batch; b0 += 8, ++launches) {
         GemvArgs a;
         a.w = m->out_w;
         a.wtype = c.out_wtype;
         a.N = c.vocab;
         a.K = d;
-        a.x = (const char *)m->x + ((size_t)b0 * last_row_stride + (last_row_stride - 1)) * d * es;
+        a.x = (const char *)xlast + ((size_t)b0 * last_row_stride + (last_row_stride - 1)) * d * es;
         a.ldx = (long)last_row_stride * d;
         a.M = batch - b0 < 8 ? batch - b0 : 8;
         a.norm_w = m->out_norm;
@@ -501,9 +554,9 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
     if (m->sampling && !m->tp) {
         // the draw replaces the argmax; RNG step = the position of each sequence's last row
         SampleArgs sp = m->sample;
-        sp.pos = pos;
-        sp.pos_stride = last_row_stride;
-        sp.pos_off = last_row_stride - 1;
+        sp.pos = pg ? pg->last_pos : pos;
+        sp.pos_stride = pg ? 1 : last_row_stride;
+        sp.pos_off = pg ? 0 : last_row_stride - 1;
         sample_rows(tokens, m->logits, c.vocab, batch, c.vocab, m->act, sp, s);
         ++launches;
     }
@@ -679,6 +732,10 @@ void wk_model_destroy(wk_model *m) {
                     m->attn_ws.minv, m->logits};
     for (void *p : bufs)
         if (p) cudaFree(p);
+    if (m->d_meta) cudaFree(m->d_meta);
+    free(m->row_slot);
+    free(m->slot_pos);
+    free(m->slot_used);
     free(m->layers);
     delete m;
 }
@@ -726,6 +783,10 @@ int wk_model_alloc_cache(wk_model *m, int max_batch, int max_ctx) {
     fill_block_table(m->block_table, max_batch, m->max_pages, s);
     for (int **p : {&m->d_pos, &m->d_seq, &m->d_ids, &m->d_tokens}) WK_TRY(cudaMallocAsync(p, sizeof(int) * max_batch, s));
     iota_kernel<<<(max_batch + 127) / 128, 128, 0, s>>>(m->d_seq, max_batch, 0, 1);
+    m->row_slot = (int *)calloc(max_batch, sizeof(int));
+    m->slot_pos = (int *)calloc(max_batch, sizeof(int));
+    m->slot_used = (unsigned char *)calloc(max_batch, 1);
+    WK_TRY(cudaMallocAsync(&m->d_meta, sizeof(int) * 4 * max_batch, s));
     WK_TRY(cudaGetLastError());
     {
         // split-K decode attention: up to 64 splits of the context per (sequence, kv head)
@@ -808,6 +869,15 @@ int wk_model_prefill(wk_model *m, const int *ids, int batch, int n, int *tokens_
     fill_i32_kernel<<<(batch + 127) / 128, 128, 0, s>>>(m->d_pos, batch, n);
     WK_TRY(cudaGetLastError());
     if (tokens_out) WK_TRY(cudaMemcpyAsync(tokens_out, m->d_tokens, sizeof(int) * batch, cudaMemcpyDeviceToDevice, s));
+    // the batch is the sequences of slots 0..batch-1, in order
+    iota_kernel<<<(batch + 127) / 128, 128, 0, s>>>(m->d_seq, batch, 0, 1);
+    WK_TRY(cudaGetLastError());
+    memset(m->slot_used, 0, m->max_batch);
+    for (int b = 0; b < batch; ++b) {
+        m->row_slot[b] = b;
+        m->slot_pos[b] = n;
+        m->slot_used[b] = 1;
+    }
     if (m->graph && m->graph_batch != batch) {
         cudaGraphExecDestroy(m->graph);
         m->graph = nullptr;
@@ -817,6 +887,127 @@ int wk_model_prefill(wk_model *m, const int *ids, int batch, int n, int *tokens_
     return 0;
 }
 
+// the longest active sequence (the context bound of the next step)
+static int longest(const wk_model *m) {
+    int p = 0;
+    for (int r = 0; r < m->batch; ++r) p = m->slot_pos[m->row_slot[r]] > p ? m->slot_pos[m->row_slot[r]] : p;
+    return p;
+}
+
+int wk_model_add_seqs(wk_model *m, const int *ids, const int *lens, int count, int *slots_out) {
+    if (!m || !m->kpool) return fail("cache not allocated");
+    if (device_error_pending()) return -1;
+    if (m->tp) return fail("wk_model_add_seqs: not with tensor parallelism");
+    if (count <= 0 || !ids || !lens || m->batch + count > m->max_batch)
+        return fail("wk_model_add_seqs: %d sequences do not fit beside %d of %d", count, m->batch, m->max_batch);
+    int rows = 0, longest_new = 0;
+    for (int i = 0; i < count; ++i) {
+        if (lens[i] <= 0 || lens[i] > m->max_ctx || lens[i] > m->freqs_ctx)
+            return fail("wk_model_add_seqs: length %d outside [1, %d]", lens[i], m->max_ctx);
+        rows += lens[i];
+        longest_new = lens[i] > longest_new ? lens[i] : longest_new;
+    }
+    set_device_current();
+    cudaStream_t s = stream();
+    if (ensure_rows(m, rows < 8 * m->max_batch ? 8 * m->max_batch : rows)) return -1;
+    // free slots, lowest first
+    int *slot = (int *)malloc(sizeof(int) * count * 3), *row0 = slot + count;
+    int *meta = (int *)malloc(sizeof(int) * (2 * rows + 2 * count));
+    int *rseq = meta, *rpos = meta + rows, *lrow = meta + 2 * rows, *lpos = lrow + count;
+    for (int i = 0, sl = 0; i < count; ++i) {
+        while (m->slot_used[sl]) ++sl;
+        slot[i] = sl++;
+    }
+    for (int i = 0, r = 0; i < count; ++i) {
+        row0[i] = r;
+        for (int j = 0; j < lens[i]; ++j, ++r) {
+            rseq[r] = slot[i];
+            rpos[r] = j;
+        }
+        lrow[i] = r - 1;
+        lpos[i] = lens[i] - 1;
+    }
+    // per-row slot and position, then each new sequence's last row and its position
+    cudaError_t e = cudaMemcpyAsync(m->d_row_seq, rseq, sizeof(int) * rows, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->d_row_pos, rpos, sizeof(int) * rows, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->d_meta, lrow, sizeof(int) * 2 * count, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+        free(slot);
+        free(meta);
+        return fail("wk_model_add_seqs: %s", cudaGetErrorString(e));
+    }
+    PrefillGroups pg;
+    pg.count = count;
+    pg.row0 = row0;
+    pg.len = lens;
+    pg.slot = slot;
+    pg.last_rows = m->d_meta;
+    pg.last_pos = m->d_meta + count;
+    const int B0 = m->batch;
+    launch_embed(m, ids, rows);
+    run_layers(m, rows, m->d_row_seq, m->d_row_pos, longest_new, count, 1, m->d_tokens + B0, &pg);
+    // the new rows join the decode batch: next input = the generated token at position len
+    for (int i = 0; i < count; ++i) {
+        m->row_slot[B0 + i] = slot[i];
+        m->slot_pos[slot[i]] = lens[i];
+        m->slot_used[slot[i]] = 1;
+        if (slots_out) slots_out[i] = slot[i];
+    }
+    int *hostv = (int *)malloc(sizeof(int) * 2 * count);
+    for (int i = 0; i < count; ++i) {
+        hostv[i] = slot[i];
+        hostv[count + i] = lens[i];
+    }
+    e = cudaMemcpyAsync(m->d_seq + B0, hostv, sizeof(int) * count, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->d_pos + B0, hostv + count, sizeof(int) * count, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->d_ids + B0, m->d_tokens + B0, sizeof(int) * count, cudaMemcpyDeviceToDevice, s);
+    free(hostv);
+    free(slot);
+    free(meta);
+    if (e != cudaSuccess) return fail("wk_model_add_seqs: %s", cudaGetErrorString(e));
+    m->batch = B0 + count;
+    m->pos = longest(m);
+    if (m->graph && m->graph_batch != m->batch) {
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    return 0;
+}
+
+int wk_model_remove_seq(wk_model *m, int slot) {
+    if (!m || !m->kpool) return fail("cache not allocated");
+    if (slot < 0 || slot >= m->max_batch || !m->slot_used[slot]) return fail("wk_model_remove_seq: slot %d is not in use", slot);
+    set_device_current();
+    cudaStream_t s = stream();
+    int r = 0;
+    while (m->row_slot[r] != slot) ++r;
+    const int L = m->batch - 1;
+    if (r != L) {
+        // the last row takes the freed row's place
+        m->row_slot[r] = m->row_slot[L];
+        for (int *p : {m->d_seq, m->d_pos, m->d_ids, m->d_tokens})
+            WK_TRY(cudaMemcpyAsync(p + r, p + L, sizeof(int), cudaMemcpyDeviceToDevice, s));
+    }
+    m->slot_used[slot] = 0;
+    m->batch = L;
+    m->pos = longest(m);
+    if (m->graph) {
+        WK_TRY(cudaStreamSynchronize(s));
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    return 0;
+}
+
+int wk_model_rows(const wk_model *m, int *slots) {
+    if (!m) return 0;
+    if (slots)
+        for (int r = 0; r < m->batch; ++r) slots[r] = m->row_slot[r];
+    return m->batch;
+}
+
 int wk_model_decode_step(wk_model *m) {
     if (!m || m->batch <= 0) return fail("no armed batch (call wk_model_prefill first)");
     if (m->pos + 1 > m->max_ctx || m->pos + 1 > m->freqs_ctx) return fail("context full (%d)", m->pos);
@@ -824,6 +1015,12 @@ int wk_model_decode_step(wk_model *m) {
     set_device_current();
     cudaStream_t s = stream();
     const int B = m->batch;
+    for (int r = 0; r < B; ++r) ++m->slot_pos[m->row_slot[r]];
+    if (m->graph && m->graph_batch != B) {
+        WK_TRY(cudaStreamSynchronize(s));
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
     if (m->mk_mode < 0) mk_setup(m);
     if (m->mk_mode == 1 && B <= 8 && !m->sampling) {
         if (ensure_rows(m, 8 * B)) return -1;
@@ -841,7 +1038,7 @@ int wk_model_decode_step(wk_model *m) {
         if (e == cudaSuccess) {
             m->mk_base += (unsigned long long)mk_barriers(m->cfg.n_layers) * g_rt.num_sms;
             m->step_launches = 1;
-            m->pos += 1;
+            m->pos = longest(m);
             return 0;
         }
         // the device cannot co-schedule it: use the graph path from now on
@@ -869,7 +1066,7 @@ int wk_model_decode_step(wk_model *m) {
         m->step_launches = n;
     }
     WK_TRY(cudaGraphLaunch(m->graph, s));
-    m->pos += 1;
+    m->pos = longest(m);
     return 0;
 }
 
@@ -880,11 +1077,15 @@ int wk_model_position(const wk_model *m) { return m ? m->pos : 0; }
 
 int wk_model_truncate(wk_model *m, int n) {
     if (!m || m->batch <= 0) return fail("no armed batch (call wk_model_prefill first)");
-    if (n < 1 || n > m->pos) return fail("truncate to %d outside [1, %d]", n, m->pos);
+    int shortest = m->pos;
+    for (int r = 0; r < m->batch; ++r)
+        shortest = m->slot_pos[m->row_slot[r]] < shortest ? m->slot_pos[m->row_slot[r]] : shortest;
+    if (n < 1 || n > shortest) return fail("truncate to %d outside [1, %d]", n, shortest);
     set_device_current();
     cudaStream_t s = stream();
     fill_i32_kernel<<<(m->batch + 127) / 128, 128, 0, s>>>(m->d_pos, m->batch, n);
     WK_TRY(cudaGetLastError());
+    for (int r = 0; r < m->batch; ++r) m->slot_pos[m->row_slot[r]] = n;
     m->pos = n;
     return 0;
 }
