@@ -37,7 +37,7 @@ constexpr int kThreads = 320;
 constexpr int kMaxSlots = 6;                    // 64-k operand stages (deepest ring)
 // operand ring depth: 4 stages of 128-token B tiles fit beside the raw ring, 6 of 64 / 32
 template <int BN> struct Slots {
-    static constexpr int n = BN >= 128 ? 4 : 6;
+    static constexpr int n = BN >= 256 ? 3 : (BN >= 128 ? 4 : 6);
 };
 constexpr int kRawSlots = 2;                    // 256-k raw Q8_0 stages
 constexpr int kATileBytes = 128 * 128;          // 128 rows x 64 halves
@@ -572,8 +572,10 @@ void gemm_tc(GemmArgs a, int act, cudaStream_t s) {
     if (!a.err) a.err = g_rt.d_error;
     const size_t es = 2;
     // activations: [M rows][K] with row stride ldx, boxes of 64 k x BN rows, 128-byte swizzle
-    // token tile: 128 only for long blocks; 64 for M >= 48 so that M = 128 spreads over twice the CTAs
-    const int BN = a.M >= 256 ? 128 : (a.M >= 48 ? 64 : 32);
+    // token tile: 64 for M >= 48 so that M = 128 spreads over twice the CTAs
+    // 256-token tiles for long blocks (half the operand traffic per FLOP of 128-token
+    // tiles: the main loop is bound by operand loads, not by the tensor core)
+    const int BN = a.M >= 1024 ? 256 : a.M >= 256 ? 128 : (a.M >= 48 ? 64 : 32);
     if (((uintptr_t)a.x % 16) || ((a.ldx * es) % 16)) WK_PANIC("gemm_tc: activations must be 16-byte aligned rows");
     if (!encode_map_2d(&a.xmap, a.x, act == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                        (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.ldx * es, 64, (uint32_t)BN,
@@ -605,7 +607,9 @@ void gemm_tc(GemmArgs a, int act, cudaStream_t s) {
     const bool pdl = g_rt.pdl && a.pdl;
 #define WK_TC_LAUNCH(T, W)                        \
     do {                                          \
-        if (BN == 128)                            \
+        if (BN == 256)                            \
+            launch_tc<T, W, 256>(a, s, pdl);      \
+        else if (BN == 128)                       \
             launch_tc<T, W, 128>(a, s, pdl);      \
         else if (BN == 64)                        \
             launch_tc<T, W, 64>(a, s, pdl);       \
