@@ -144,7 +144,9 @@ def run_ours(args, rank, world, local_rank):
     e2e_abi = not args.no_e2e and tpw == 1
     # the engine e2e leg (tensor-parallel runs) continues decoding after the timed steps
     ctx = P + W + K + 8 + (W + K if (not args.no_e2e and not e2e_abi) else 0)
-    sm = SyntheticLlama(cfg, ctx, seed=SEED, unfused=e2e_abi, tp_rank=rank if tpw > 1 else 0, tp_world=tpw)
+    wt = wk.F16 if args.wtype == "f16" else wk.Q8_0
+    sm = SyntheticLlama(cfg, ctx, wtype=wt, out_type=wt, seed=SEED, unfused=e2e_abi, tp_rank=rank if tpw > 1 else 0,
+                        tp_world=tpw)
     eng = Engine.from_synthetic(sm, max_batch=B, tp=tpw > 1)
     prompt = np.random.default_rng(7).integers(0, cfg["V"], size=(B, P)).astype(np.int32)
     d_prompt = L.cuda_malloc(prompt.nbytes)
@@ -195,8 +197,8 @@ def run_ours(args, rank, world, local_rank):
     # dominant kernel: the Q8_0 dequant-GEMV at the FFN up|gate shape of the
     # model (per rank), timed alone over 8 rotating weight copies (> L2)
     if rank == 0:
-        res["gemv"] = time_gemv(L, stream, N=2 * sm.local["F"], K=cfg["d"], M=B)
-        res["gemv_op"] = time_gemv(L, stream, N=8192, K=2048, M=B)
+        res["gemv"] = time_gemv(L, stream, N=2 * sm.local["F"], K=cfg["d"], M=min(B, 8), wtype=wt)
+        res["gemv_op"] = time_gemv(L, stream, N=8192, K=2048, M=min(B, 8), wtype=wt)
 
     if not args.no_e2e:
         if e2e_abi:
@@ -211,23 +213,26 @@ def run_ours(args, rank, world, local_rank):
     return res
 
 
-def time_gemv(L, stream, N, K, M, copies=8, reps=20):
+def time_gemv(L, stream, N, K, M, copies=8, reps=20, wtype=8):
     import torch
-    rb = N * (K // 32) * 34
+    rb = N * (K // 32) * 34 if wtype == 8 else N * K * 2
     ws = [L.cuda_malloc(rb) for _ in range(copies)]
     for i, p in enumerate(ws):
-        L.wk_fill_random_q8_0(p, N, K, 77 + i, 0.02)
+        if wtype == 8:
+            L.wk_fill_random_q8_0(p, N, K, 77 + i, 0.02)
+        else:
+            L.wk_fill_random_f16(p, N * K, 77 + i, 0.02)
     x = L.cuda_malloc(2 * M * K)
     L.wk_fill_random_f16(x, M * K, 5, 1.0)
     o = L.cuda_malloc(2 * M * N)
     for i in range(3):
-        L.wk_gemv(o, x, ws[i % copies], M, K, N, 8)
+        L.wk_gemv(o, x, ws[i % copies], M, K, N, wtype)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     n = reps * copies
     for i in range(n):
-        L.wk_gemv(o, x, ws[i % copies], M, K, N, 8)
+        L.wk_gemv(o, x, ws[i % copies], M, K, N, wtype)
     e1.record(stream)
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000 / n
@@ -406,7 +411,7 @@ def run_prefill(args):
 
 
 # ------------------------------------------------------------------ CPU baseline
-def run_cpu(model, B, P, steps, budget_s=25.0):
+def run_cpu(model, B, P, steps, budget_s=25.0, wtype=8):
     """The oracle port (C++ restatement of the reference semantics) on the host
     cores, on the same synthetic model (the oracle's generator is bit-identical
     to the device one): prefill the prompt, then time greedy decode steps until
@@ -419,8 +424,8 @@ def run_cpu(model, B, P, steps, budget_s=25.0):
     # 8B: a 128-token prompt instead of 2048 keeps the CPU prefill to seconds;
     # a decode step there is bound by the 8 GB of weights, not by the context
     P_full, P = P, (P if model == "1b" else min(P, 128))
-    w = make_weights(cfg, 8, 8, 1, seed=SEED, ctx=P + steps + 16)
-    om = oracle_model(w, cfg, 8, 8, 1, P + steps + 16)
+    w = make_weights(cfg, wtype, wtype, 1, seed=SEED, ctx=P + steps + 16)
+    om = oracle_model(w, cfg, wtype, wtype, 1, P + steps + 16)
     om.reset(B)
     prompt = np.random.default_rng(7).integers(0, cfg["V"], size=(B, P)).astype(np.int32)
     tok, _, _ = om.forward(prompt)
@@ -431,7 +436,8 @@ def run_cpu(model, B, P, steps, budget_s=25.0):
         n += 1
     dt = time.perf_counter() - t0
     return dict(value=B * n / dt, unit="tokens/s", cores=orc.num_threads(), kind="port",
-                sample=f"{n} decode steps after a {P}-token prefill, batch {B}, {NAMES[model]} Q8_0"
+                sample=f"{n} decode steps after a {P}-token prefill, batch {B}, {NAMES[model]} "
+                       f"{'Q8_0' if wtype == 8 else 'F16'}"
                        + ("" if P == P_full else f" (the GPU arm's prompt is {P_full} tokens)"))
 
 
@@ -453,7 +459,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="decode", choices=["decode", "prefill"],
                     help="prefill: time wk_model_prefill of --batch prompts of --prompt tokens (one JSON line)")
-    ap.add_argument("--wtype", default="q8_0", choices=["q8_0", "f16"], help="linear / output weights (--mode prefill)")
+    ap.add_argument("--wtype", default="q8_0", choices=["q8_0", "f16"], help="linear and output weights")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--op", default=None, metavar="NxKxM[,...]",
@@ -472,6 +478,9 @@ def main():
         args.model = "8b" if (launched or world > 1 or args.gpus > 1) else "1b"
     if args.prompt is None:
         args.prompt = PROMPTS[args.model]
+    dtype_str = "int8 x f16 -> f32" if args.wtype == "q8_0" else "f16 x f16 -> f32"
+    metric = METRIC if (args.batch == 1 and args.wtype == "q8_0") else \
+        f"decode tokens/sec (batch {args.batch}, {args.wtype.upper()})"
     tp = args.model != "1b" and world > 1
     if tp:
         par = f"tp{world}"
@@ -479,9 +488,11 @@ def main():
         par = f"replicas x{world}"
     else:
         par = "single GPU"
-    config = {"workload": f"{NAMES[args.model]} Q8_0 greedy decode, batch {args.batch}, {args.prompt}-token prompt",
+    config = {"workload": f"{NAMES[args.model]} {args.wtype.upper()} greedy decode, batch {args.batch}, "
+                          f"{args.prompt}-token prompt",
               "model": NAMES[args.model], "batch": args.batch, "prompt": args.prompt, "decode_steps": args.steps,
-              "weights": "Q8_0 linear layers and output.weight, token_embd F16, norms 1.0, w ~ N(0, 0.02), "
+              "weights": f"{args.wtype.upper()} linear layers and output.weight, token_embd F16, norms 1.0, "
+                         "w ~ N(0, 0.02), "
                          "generated on the device",
               "l2": "weights read per step exceed the 126 MB L2, no flush", "parallelism": par,
               "timing": f"median of identical timed blocks of {args.steps} decode steps, each from the same "
@@ -501,9 +512,10 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "the 70B CPU restatement needs about 80 GB of "
                               "host memory for its weights; no CPU run at this size"}))
             return
-        cpu = run_cpu(args.model, args.batch, args.prompt, args.warmup + args.steps, budget_s=150.0)
-        line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": "tokens/s", "n_gpus": 1,
-                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "int8 x f16 -> f32",
+        cpu = run_cpu(args.model, args.batch, args.prompt, args.warmup + args.steps, budget_s=150.0,
+                      wtype=8 if args.wtype == "q8_0" else 1)
+        line = {"impl": "reference", "metric": metric, "value": cpu["value"], "unit": "tokens/s", "n_gpus": 1,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": dtype_str,
                 "data": "synthetic", "config": config,
                 "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -528,16 +540,16 @@ def main():
     K = args.steps
     value = (1 if tp else world) * args.batch * K / (res["ms"] / 1e3)
     g = res["gemv"]
-    gname = f"gemv_q8_0_{g['N']}x{g['K']}_m{g['M']}"
+    gname = f"gemv_{args.wtype}_{g['N']}x{g['K']}_m{g['M']}"
     step_gbs = res["step_bytes"] / (res["ms"] / K) / 1e6
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
+        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
         "ms_per_step": res["ms"] / K, "timed_blocks": res["blocks"],
         "block_ms": {"median": res["ms"], "min": res["block_ms_min"], "max": res["block_ms_max"]},
         "higher_is_better": True, "scaling": "strong" if tp else "weak",
-        "vs_baseline": None, "dtype": "int8 x f16 -> f32", "data": "synthetic", "config": config,
+        "vs_baseline": None, "dtype": dtype_str, "data": "synthetic", "config": config,
         "gpu_launches": res["launches"] * K,
-        "roofline": {"bound": "hbm", "kernel": f"gemv_kernel<Q8_0> {g['N']}x{g['K']} M={g['M']}",
+        "roofline": {"bound": "hbm", "kernel": f"gemv_kernel<{args.wtype.upper()}> {g['N']}x{g['K']} M={g['M']}",
                      "achieved": g["gbs"], "peak": hbm, "unit": "GB/s", "frac": g["gbs"] / hbm,
                      "peak_source": src, "traffic": profiled_traffic(gname),
                      "step": {"bytes_per_gpu": res["step_bytes"], "achieved": step_gbs, "frac": step_gbs / hbm}},
@@ -546,8 +558,8 @@ def main():
     }
     if "e2e" in res:
         line["e2e"] = res["e2e"]
-    if not args.no_cpu and world == 1 and args.model == "1b":
-        cpu = run_cpu(args.model, args.batch, args.prompt, 64)
+    if not args.no_cpu and world == 1 and args.model in ("1b", "8b"):
+        cpu = run_cpu(args.model, args.batch, args.prompt, 64, wtype=8 if args.wtype == "q8_0" else 1)
         line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
     print(json.dumps(line))
 

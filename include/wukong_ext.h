@@ -68,6 +68,9 @@ int wk_model_decode_step(wk_model *m);
 int wk_model_add_seqs(wk_model *m, const int *ids, const int *lens, int count, int *slots_out);
 int wk_model_remove_seq(wk_model *m, int slot);
 int wk_model_rows(const wk_model *m, int *slots);
+/* device [batch, vocab] logits (activation dtype) of the latest step's last
+ * rows while sampling is on (wk_model_set_sampling), else null */
+const void *wk_model_logits(const wk_model *m);
 /* device int32 [batch]: tokens produced by the latest prefill / decode step */
 const int *wk_model_tokens(const wk_model *m);
 /* device int32 [batch]: input tokens of the next decode step (writable) */

@@ -45,7 +45,8 @@ def test_q4_0_device_generator_and_dequantise_bit_exact(dev):
     wk.check(dev.wk_fill_random_q4_0(p, rows, cols, 123, 0.02))
     got = down(p, rows * cols // 32 * 18, np.uint8)
     want = orc.gen_q4_0(rows, cols, 123, 0.02)
-    assert np.array_equal(got, want)
+    bad = np.flatnonzero(got != want)
+    assert bad.size == 0, (bad.size, bad[:8].tolist(), got[bad[:8]].tolist(), want[bad[:8]].tolist())
     o = alloc(4 * rows * cols)
     dev.cuda_dequantize(o, p, rows, cols, wk.Q4_0)
     assert np.array_equal(down(o, (rows, cols), np.float32), orc.dequant_q4_0(want, rows, cols))

@@ -94,9 +94,11 @@ def test_cuda_sampler_matches_restatement(dev, t, k, p):
 def test_engine_sampling_vs_oracle(dev):
     """The engine with sampling on (prefill + decode steps feeding the drawn
     token back on the device) against the oracle run on the engine's tokens:
-    the same draw wherever the oracle's u is not within 2e-3 of a prefix-sum
-    boundary (the two sides' logits differ by fp32 summation order); the same
-    seed reproduces the tokens, another seed changes them."""
+    the same draw wherever the oracle's u is not within 1e-2 of a prefix-sum
+    boundary (the two sides' logits differ by fp32 summation order, which moves
+    the prefix sums by up to ~1e-2); the engine's draw equals the rule applied
+    to the engine's own logits; the same seed reproduces the tokens, another
+    seed changes them."""
     from tests.gpu_util import alloc, down, free, up
     from tests.model_util import LLAMA_1B, DeviceModel, build_engine, make_weights, oracle_model
     cfg = dict(LLAMA_1B, L=2)
@@ -112,23 +114,30 @@ def test_engine_sampling_vs_oracle(dev):
         pids, ptok = up(ids), alloc(4)
         wk.check(dev.wk_model_prefill(m, pids, 1, n, ptok))
         toks = [int(down(ptok, 1, np.int32)[0])]
+        lg = [down(dev.wk_model_logits(m), (1, cfg["V"]), np.float16).astype(np.float32)]
         for _ in range(steps):
             wk.check(dev.wk_model_decode_step(m))
             toks.append(int(down(dev.wk_model_tokens(m), 1, np.int32)[0]))
+            lg.append(down(dev.wk_model_logits(m), (1, cfg["V"]), np.float16).astype(np.float32))
         dev.wk_model_destroy(m)
         free(pids, ptok)
-        return toks
+        return toks, lg
 
-    a, b, c = run(SEED), run(SEED), run(SEED + 1)
+    (a, la), (b, _), (c, _) = run(SEED), run(SEED), run(SEED + 1)
     assert a == b
     assert a != c
+    # the draw inside the engine is the sampling rule applied to the engine's own logits
+    for s, (tok, lg) in enumerate(zip(a, la)):
+        want, ud = orc.sample(lg, T, K, P, SEED, n - 1 + s)
+        if tok != want[0]:
+            assert ud[0, 1] < 1e-5, (s, tok, want[0], ud[0])
     om = oracle_model(w, cfg, wk.Q8_0, wk.Q8_0, wk.F16, ctx)
     om.reset(1)
     _, logits, _ = om.forward(ids)
     checked = 0
     for s, tok in enumerate(a):
         want, ud = orc.sample(logits, T, K, P, SEED, n - 1 + s)
-        if ud[0, 1] > 2e-3:
+        if ud[0, 1] > 1e-2:
             assert tok == want[0], (s, tok, want[0], ud[0])
             checked += 1
         _, logits, _ = om.forward(np.array([[tok]], np.int32))

@@ -62,6 +62,7 @@ EXT = {
     "wk_model_prefill": (_I, [_P, _P, _I, _I, _P]),
     "wk_model_decode_step": (_I, [_P]),
     "wk_model_tokens": (_P, [_P]),
+    "wk_model_logits": (_P, [_P]),
     "wk_model_next_ids": (_P, [_P]),
     "wk_model_step_launches": (_I, [_P]),
     "wk_model_position": (_I, [_P]),

@@ -126,15 +126,19 @@ __global__ void fill_q4_0_kernel(uint8_t *dst, long nblk, uint64_t seed, float k
     const float d = mx / -8.0f;
     const float id = d != 0.f ? 1.0f / d : 0.f;
     const unsigned short bits = __half_as_ushort(__float2half_rn(d));
-    uint8_t *o = dst + b * kQ4Bytes;
-    o[0] = (uint8_t)(bits & 0xff);
-    o[1] = (uint8_t)(bits >> 8);
+    uint8_t blk[kQ4Bytes];
+    blk[0] = (uint8_t)(bits & 0xff);
+    blk[1] = (uint8_t)(bits >> 8);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        const int n0 = min(15, (int)(x[i] * id + 8.5f));
-        const int n1 = min(15, (int)(x[i + 16] * id + 8.5f));
-        o[2 + i] = (uint8_t)(n0 | (n1 << 4));
+        // separately rounded product and sum (no fused multiply-add), as the host rule
+        const int n0 = min(15, (int)__fadd_rn(__fmul_rn(x[i], id), 8.5f));
+        const int n1 = min(15, (int)__fadd_rn(__fmul_rn(x[i + 16], id), 8.5f));
+        blk[2 + i] = (uint8_t)(n0 | (n1 << 4));
     }
+    volatile uint8_t *o = dst + b * kQ4Bytes;
+#pragma unroll
+    for (int i = 0; i < kQ4Bytes; ++i) o[i] = blk[i];
 }
 
 __global__ void fill_f16_kernel(__half *dst, long n, uint64_t seed, float k) {
@@ -1071,6 +1075,7 @@ int wk_model_decode_step(wk_model *m) {
 }
 
 const int *wk_model_tokens(const wk_model *m) { return m ? m->d_tokens : nullptr; }
+const void *wk_model_logits(const wk_model *m) { return m && m->sampling ? m->logits : nullptr; }
 int *wk_model_next_ids(wk_model *m) { return m ? m->d_ids : nullptr; }
 int wk_model_step_launches(const wk_model *m) { return m ? m->step_launches : 0; }
 int wk_model_position(const wk_model *m) { return m ? m->pos : 0; }
