@@ -279,11 +279,12 @@ def _from_dev(raw, act):
 @pytest.mark.parametrize("wtype", [Q8_0, F16, BF16])
 @pytest.mark.parametrize("M,N,K", [(1, 8192, 2048), (16, 8192, 2048), (128, 8192, 2048), (5, 2048, 8192),
                                    (3, 97, 256), (8, 70, 160), (2, 48, 4096), (512, 2048, 2048),
-                                   (1100, 1024, 4096), (2048, 640, 1024)])
+                                   (1100, 1024, 4096), (2048, 640, 1024), (32, 2048, 8192), (48, 3072, 2048)])
 def test_matmul_vs_oracle(dev, wtype, M, N, K):
     """BASELINE op: W [8192 x 2048] (Q8_0: scale max|w|/127, q = round(w/scale)),
     X [M x 2048] ~ N(0, 1), M in {1, 16, 128}; plus ragged and unaligned shapes,
-    and prefill-sized blocks (128- and 256-token tiles of the tcgen05 GEMM)."""
+    prefill-sized blocks (128- and 256-token tiles of the tcgen05 GEMM) and
+    batched-decode blocks whose few output tiles split K over the SMs."""
     if wtype == Q8_0 and K % 32:
         pytest.skip("Q8_0 needs K % 32 == 0")
     act = BF16 if wtype == BF16 else F16

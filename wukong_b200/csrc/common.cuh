@@ -85,6 +85,11 @@ struct Runtime {
     // called by cuda_fini with the device index (set by parts that cache
     // per-device state; a pointer, so cuda.h's objects do not link them in)
     void (*on_fini)(int device) = nullptr;
+    // split-K workspace of the tcgen05 GEMM (all launches are ordered on `stream`)
+    float *splitk_ws = nullptr;
+    size_t splitk_ws_floats = 0;
+    int *splitk_counter = nullptr;
+    int splitk_tiles = 0;
 };
 extern Runtime g_rt;
 

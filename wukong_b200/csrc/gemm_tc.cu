@@ -311,8 +311,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tile = blockIdx.x, m0 = blockIdx.y * BN;
     const bool swiglu = a.epi == EPI_SWIGLU;
-    const int nkb = a.K / kKB;      // raw stages (Q8_0) / 4 x 64-k subs
-    const int nsub = a.K / 64;      // operand stages
+    // split-K (gridDim.z > 1): this CTA's K range [kz0, kz0 + K / gridDim.z)
+    const int Kc = a.K / (int)gridDim.z;
+    const int kz0 = (int)blockIdx.z * Kc;
+    const int nkb = Kc / kKB;       // raw stages (Q8_0) / 4 x 64-k subs
+    const int nsub = Kc / 64;       // operand stages
+    const int kb0 = kz0 / kKB, ks0 = kz0 / 64;
     constexpr bool kQ8 = WT == kQ8_0;
     constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
     constexpr uint32_t kIdesc = (1u << 4) | ((WT == kBF16 ? 1u : 0u) << 7) | ((WT == kBF16 ? 1u : 0u) << 10) |
@@ -347,10 +351,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 const int s = kb % kRawSlots;
                 mbar_expect_tx(&bars->raw_full[s], kRawBytes);
                 if (swiglu) {
-                    tma2d(RAW + (size_t)s * kRawBytes, &a.wmap, kb * 136, wy, &bars->raw_full[s]);
-                    tma2d(RAW + (size_t)s * kRawBytes + 64 * 272, &a.wmap, kb * 136, a.F + wy, &bars->raw_full[s]);
+                    tma2d(RAW + (size_t)s * kRawBytes, &a.wmap, (kb0 + kb) * 136, wy, &bars->raw_full[s]);
+                    tma2d(RAW + (size_t)s * kRawBytes + 64 * 272, &a.wmap, (kb0 + kb) * 136, a.F + wy,
+                          &bars->raw_full[s]);
                 } else {
-                    tma2d(RAW + (size_t)s * kRawBytes, &a.wmap, kb * 136, wy, &bars->raw_full[s]);
+                    tma2d(RAW + (size_t)s * kRawBytes, &a.wmap, (kb0 + kb) * 136, wy, &bars->raw_full[s]);
                 }
             };
             int raw_issued = 0;
@@ -365,13 +370,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 }
                 const uint32_t tx = (uint32_t)(L::kBTile + (kQ8 ? 0 : kATileBytes));
                 mbar_expect_tx(&bars->b_full[s], tx);
-                tma2d(B + (size_t)s * L::kBTile, &a.xmap, i * 64, m0, &bars->b_full[s]);
+                tma2d(B + (size_t)s * L::kBTile, &a.xmap, (ks0 + i) * 64, m0, &bars->b_full[s]);
                 if (!kQ8) {
                     if (swiglu) {
-                        tma2d(A + (size_t)s * kATileBytes, &a.wmap, i * 64, wy, &bars->b_full[s]);
-                        tma2d(A + (size_t)s * kATileBytes + 64 * 128, &a.wmap, i * 64, a.F + wy, &bars->b_full[s]);
+                        tma2d(A + (size_t)s * kATileBytes, &a.wmap, (ks0 + i) * 64, wy, &bars->b_full[s]);
+                        tma2d(A + (size_t)s * kATileBytes + 64 * 128, &a.wmap, (ks0 + i) * 64, a.F + wy,
+                              &bars->b_full[s]);
                     } else {
-                        tma2d(A + (size_t)s * kATileBytes, &a.wmap, i * 64, wy, &bars->b_full[s]);
+                        tma2d(A + (size_t)s * kATileBytes, &a.wmap, (ks0 + i) * 64, wy, &bars->b_full[s]);
                     }
                 }
                 // keep the raw ring one stage ahead of the operand stages
@@ -460,7 +466,59 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         const bool acc_ok = ok && mbar_wait_bounded(&bars->acc_full, 0, err, 16);
         tc_fence_after();
         float *xchg = reinterpret_cast<float *>(RAW);  // [128 rows][32 columns] for row pairing
-        if (a.vec) {
+        // split-K: every split stores its fp32 tile ([128 rows][BN] per split and
+        // tile); the last split of the tile to arrive adds them in split order
+        // (the same sum whatever the arrival order) and runs the epilogue
+        const int nz = (int)gridDim.z;
+        const long tile_id = (long)blockIdx.y * gridDim.x + blockIdx.x;
+        bool run_epi = true;
+        if (nz > 1) {
+            float *mine = a.ws + ((tile_id * nz + blockIdx.z) * 128 + row) * BN;
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t v[32];
+                tc_ld32(tmem + (((uint32_t)(warp & 3) * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                    *reinterpret_cast<float4 *>(mine + c0 + i) =
+                        acc_ok ? make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]),
+                                             __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            __threadfence();
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            __shared__ int s_last;
+            if (threadIdx.x == 64) s_last = atomicAdd(a.ws_counter + tile_id, 1) == nz - 1;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            run_epi = s_last != 0;
+            if (run_epi) __threadfence();
+        }
+        // the tile's accumulators for 32 tokens from c0: TMEM, or the splits' sum
+        auto load_acc = [&](int c0, uint32_t (&v)[32]) {
+            if (nz == 1) {
+                tc_ld32(tmem + (((uint32_t)(warp & 3) * 32) << 16) + (uint32_t)c0, v);
+                if (!acc_ok)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = 0u;
+                return;
+            }
+            float acc[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+            for (int z = 0; z < nz; ++z) {
+                const float4 *src = reinterpret_cast<const float4 *>(a.ws + ((tile_id * nz + z) * 128 + row) * BN + c0);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 f = __ldcg(src + i);
+                    acc[4 * i] += f.x;
+                    acc[4 * i + 1] += f.y;
+                    acc[4 * i + 2] += f.z;
+                    acc[4 * i + 3] += f.w;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(acc[i]);
+        };
+        if (run_epi && a.vec) {
             // the accumulators of 32 tokens go through shared memory ([32 tokens][128 rows]
             // fp32) so that each thread then handles 16-byte groups of 8 consecutive outputs
             float *st = reinterpret_cast<float *>(RAW);
@@ -468,10 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             const int groups = swiglu ? 8 : 16;  // 8-row groups per token (SwiGLU: the 64 up rows)
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 uint32_t v[32];
-                tc_ld32(tmem + (((uint32_t)(warp & 3) * 32) << 16) + (uint32_t)c0, v);
-                if (!acc_ok)
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = 0u;
+                load_acc(c0, v);
                 asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous chunk's groups are done
 #pragma unroll
                 for (int i = 0; i < 32; ++i) st[i * 128 + row] = __uint_as_float(v[i]);
@@ -496,13 +551,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 }
             }
         }
-        for (int c0 = 0; !a.vec && c0 < BN; c0 += 32) {
+        for (int c0 = 0; run_epi && !a.vec && c0 < BN; c0 += 32) {
             uint32_t v[32];
-            const uint32_t taddr = tmem + (((uint32_t)(warp & 3) * 32) << 16) + (uint32_t)c0;
-            tc_ld32(taddr, v);
-            if (!acc_ok)
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = 0u;
+            load_acc(c0, v);
             // pairing partner (RoPE: row ^ 1 in the neighbouring lane; SwiGLU: row + 64)
             if (swiglu) {
                 asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -521,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
                 if (row_ok && m < a.M) store_out<T>(a, n, m, __uint_as_float(v[i]), &pv);
             }
         }
+        if (nz > 1 && run_epi && threadIdx.x == 64) a.ws_counter[tile_id] = 0;  // ready for the next launch
         }  // half == 0: the epilogue warps
     }
     tc_fence_before();
@@ -541,7 +593,7 @@ template <typename T, int WT, int BN> void launch_tc(const GemmArgs &a, cudaStre
     }
     const int ntiles = a.epi == EPI_SWIGLU ? (a.F + 63) / 64 : (a.N + 127) / 128;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ntiles, (a.M + BN - 1) / BN);
+    cfg.gridDim = dim3(ntiles, (a.M + BN - 1) / BN, a.ksplit);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -604,6 +656,21 @@ void gemm_tc(GemmArgs a, int act, cudaStream_t s) {
             (a.epi != EPI_STORE || al16(a.bias, 0, es)) &&
             (a.epi != EPI_QKV || (a.hd % 8 == 0 && a.nq % 8 == 0 && a.nk % 8 == 0 && al16(a.kpool, 0, es) &&
                                   al16(a.vpool, 0, es)));
+    // split-K when the output tiles would leave most SMs idle (small batches):
+    // up to one CTA per SM, each K slice a multiple of 256
+    a.ksplit = 1;
+    {
+        const long tiles = (long)(a.epi == EPI_SWIGLU ? (a.F + 63) / 64 : (a.N + 127) / 128) * ((a.M + BN - 1) / BN);
+        if (BN <= 64 && g_rt.splitk_ws && tiles * 2 <= g_rt.num_sms) {
+            int z = (int)(g_rt.num_sms / tiles);
+            while (z > 1 && (a.K % (z * kKB) || (size_t)tiles * z * 128 * BN > g_rt.splitk_ws_floats ||
+                             tiles > g_rt.splitk_tiles))
+                --z;
+            a.ksplit = z;
+        }
+        a.ws = g_rt.splitk_ws;
+        a.ws_counter = g_rt.splitk_counter;
+    }
     const bool pdl = g_rt.pdl && a.pdl;
 #define WK_TC_LAUNCH(T, W)                        \
     do {                                          \

@@ -95,6 +95,12 @@ void cuda_init(int idx) {
     if (wt && atoi(wt) > 0) g_rt.warp_tile_min = atoi(wt);
     const char *wl = getenv("WUKONG_WAIT_LIMIT_MS");
     if (wl && atoi(wl) > 0) g_rt.wait_limit_ns = 1000000ull * (unsigned long long)atoi(wl);
+    // split-K partials of the tcgen05 GEMM: at most 2 CTAs per SM of 128 x 64 fp32 tiles
+    g_rt.splitk_tiles = 1024;
+    g_rt.splitk_ws_floats = (size_t)2 * g_rt.num_sms * 128 * 64;
+    WK_CHECK(cudaMalloc(&g_rt.splitk_ws, sizeof(float) * g_rt.splitk_ws_floats));
+    WK_CHECK(cudaMalloc(&g_rt.splitk_counter, sizeof(int) * g_rt.splitk_tiles));
+    WK_CHECK(cudaMemset(g_rt.splitk_counter, 0, sizeof(int) * g_rt.splitk_tiles));
     printf("Running on GPU %d: %s, Compute Capability %d.%d\n", idx, prop.name, prop.major, prop.minor);
     fflush(stdout);
     layers_init();
@@ -108,6 +114,10 @@ void cuda_fini(void) {
     WK_CHECK(cudaStreamSynchronize(g_rt.stream));
     if (g_rt.on_fini) g_rt.on_fini(g_rt.device);
     if (g_rt.ws) WK_CHECK(cudaFree(g_rt.ws));
+    if (g_rt.splitk_ws) WK_CHECK(cudaFree(g_rt.splitk_ws));
+    if (g_rt.splitk_counter) WK_CHECK(cudaFree(g_rt.splitk_counter));
+    g_rt.splitk_ws = nullptr;
+    g_rt.splitk_counter = nullptr;
     g_rt.ws = nullptr;
     g_rt.ws_size = 0;
     WK_CHECK(cudaFreeHost(g_rt.h_error));

@@ -156,6 +156,9 @@ struct GemmArgs {
     int *err = nullptr;
     int pdl = 1;
     int vec = 0;  // set by gemm_tc(): the epilogue stores 8 outputs (16 bytes) per access
+    int ksplit = 1;              // set by gemm_tc(): K slices (gridDim.z)
+    float *ws = nullptr;         // split-K partial tiles [tiles][ksplit][128][BN]
+    int *ws_counter = nullptr;   // [tiles] arrivals, zero between launches
 };
 bool gemm_tc_supported(int wtype, int act, int K, int N, int epi, int F);
 void gemm_tc(GemmArgs a, int act, cudaStream_t s);
