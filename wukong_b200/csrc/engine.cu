@@ -125,20 +125,18 @@ __global__ void fill_q4_0_kernel(uint8_t *dst, long nblk, uint64_t seed, float k
     }
     const float d = mx / -8.0f;
     const float id = d != 0.f ? 1.0f / d : 0.f;
-    const unsigned short bits = __half_as_ushort(__float2half_rn(d));
-    uint8_t blk[kQ4Bytes];
-    blk[0] = (uint8_t)(bits & 0xff);
-    blk[1] = (uint8_t)(bits >> 8);
+    // the block is 2-byte aligned: nine 16-bit words (scale, then byte pairs of nibbles)
+    unsigned short *o = reinterpret_cast<unsigned short *>(dst + b * kQ4Bytes);
+    o[0] = __half_as_ushort(__float2half_rn(d));
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 16; i += 2) {
         // separately rounded product and sum (no fused multiply-add), as the host rule
-        const int n0 = min(15, (int)__fadd_rn(__fmul_rn(x[i], id), 8.5f));
-        const int n1 = min(15, (int)__fadd_rn(__fmul_rn(x[i + 16], id), 8.5f));
-        blk[2 + i] = (uint8_t)(n0 | (n1 << 4));
+        const int a0 = min(15, (int)__fadd_rn(__fmul_rn(x[i], id), 8.5f));
+        const int a1 = min(15, (int)__fadd_rn(__fmul_rn(x[i + 16], id), 8.5f));
+        const int b0 = min(15, (int)__fadd_rn(__fmul_rn(x[i + 1], id), 8.5f));
+        const int b1 = min(15, (int)__fadd_rn(__fmul_rn(x[i + 17], id), 8.5f));
+        o[1 + i / 2] = (unsigned short)((a0 | (a1 << 4)) | ((b0 | (b1 << 4)) << 8));
     }
-    volatile uint8_t *o = dst + b * kQ4Bytes;
-#pragma unroll
-    for (int i = 0; i < kQ4Bytes; ++i) o[i] = blk[i];
 }
 
 __global__ void fill_f16_kernel(__half *dst, long n, uint64_t seed, float k) {
