@@ -185,6 +185,22 @@ def test_dequantize_large_bit_exact(dev):
     free(x, o)
 
 
+def test_device_weight_generators_match_the_oracle(dev):
+    """The benchmark's weights come from the device generators: Q8_0 blocks and
+    F16 values bit-identical to the oracle's host generators."""
+    rows, cols = 300, 2048
+    nb = rows * cols // 32 * 34
+    p = alloc(nb)
+    wk.check(dev.wk_fill_random_q8_0(p, rows, cols, 123, 0.02))
+    got, want = down(p, nb, np.uint8), orc.gen_q8_0(rows, cols, 123, 0.02)
+    bad = np.flatnonzero(got != want)
+    assert bad.size == 0, (bad.size, bad[:8].tolist(), got[bad[:8]].tolist(), want[bad[:8]].tolist())
+    f = alloc(2 * rows * cols)
+    wk.check(dev.wk_fill_random_f16(f, rows * cols, 77, 0.02))
+    assert np.array_equal(down(f, rows * cols, np.uint16), orc.gen_f16(rows * cols, 77, 0.02))
+    free(p, f)
+
+
 def test_kat_repeat_qkv(dev, kat):
     t = kat["test_cuda.cu/cuda_repeat_qkv"]
     x = up(f32(t["inp"]))

@@ -95,16 +95,14 @@ __global__ void fill_q8_0_kernel(uint8_t *dst, long nblk, uint64_t seed, float k
         amax = fmaxf(amax, fabsf(x[i]));
     }
     const float d = amax / 127.0f;
-    const __half hs = __float2half_rn(d);
-    uint8_t *o = dst + b * 34;
-    const unsigned short bits = __half_as_ushort(hs);
-    o[0] = (uint8_t)(bits & 0xff);
-    o[1] = (uint8_t)(bits >> 8);
+    // the block is 2-byte aligned: seventeen 16-bit words (scale, then pairs of quants)
+    unsigned short *o = reinterpret_cast<unsigned short *>(dst + b * 34);
+    o[0] = __half_as_ushort(__float2half_rn(d));
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        float q = d != 0.f ? roundf(x[i] / d) : 0.f;
-        q = fminf(127.f, fmaxf(-127.f, q));
-        o[2 + i] = (uint8_t)(int8_t)q;
+    for (int i = 0; i < 32; i += 2) {
+        const float q0 = d != 0.f ? fminf(127.f, fmaxf(-127.f, roundf(x[i] / d))) : 0.f;
+        const float q1 = d != 0.f ? fminf(127.f, fmaxf(-127.f, roundf(x[i + 1] / d))) : 0.f;
+        o[1 + i / 2] = (unsigned short)((uint8_t)(int8_t)q0 | ((unsigned)(uint8_t)(int8_t)q1 << 8));
     }
 }
 
