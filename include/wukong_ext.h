@@ -101,6 +101,19 @@ int wk_model_set_sampling(wk_model *m, float temperature, int top_k, float top_p
 int wk_sample_logits(int *tokens, const void *logits, int rows, int vocab, int dtype, float temperature, int top_k,
                      float top_p, unsigned long long seed, long long step);
 
+/* The engine's decode attention on its own: out[rows][n_heads * head_dim] for
+ * query rows q[rows][n_heads * head_dim], row r the newest token of sequence
+ * seq[r] at position pos[r] (keys 0..pos[r]), over the paged cache kpool /
+ * vpool [pages][kv_heads][64][head_dim] with block_table[seqs][max_pages];
+ * max_len bounds every pos[r] + 1.  dtype F16 or BF16.  The kernel is the
+ * one decode steps use (a cluster of CTAs per (row, KV head); the one-CTA
+ * kernel with WUKONG_SPLIT_ATTN=0 or WUKONG_CLUSTER_ATTN=0).  No counterpart
+ * in the reference, whose attention recomputes K and V from the rows.
+ * Returns 0 or -1. */
+int wk_attention_decode(void *out, const void *q, const void *kpool, const void *vpool, const int *block_table,
+                        int max_pages, const int *seq, const int *pos, int rows, int max_len, int n_heads,
+                        int kv_heads, int head_dim, int dtype);
+
 /* Synthetic weights, bit-identical to the CPU oracle's generator:
  * Irwin-Hall(4) normal(0, stdv) samples of a counter-based hash. */
 int wk_fill_random_q8_0(void *dst, long rows, int cols, uint64_t seed, float stdv);

@@ -166,6 +166,35 @@ def gqa_sdpa(qkv, batch, row, NH, kvNH, HS, act):
     return out
 
 
+def decode_attention(q, kpool, vpool, block_table, seq, pos, NH, kvNH, HS, act):
+    """Attention of the newest token of each sequence over its cached keys,
+    with the rounding points of cuda.cu:767-852 and the softmax of :673-765:
+    s_j = T(q . k_j), e_j = exp(s_j / sqrt(HS) - max), sum of the unrounded
+    e_j, P_j = T(T(e_j) * (1 / sum)), o = T(sum_j P_j v_j).  q: [rows, NH * HS];
+    kpool / vpool: [pages, kvNH, 64, HS] (values on the grid of `act`);
+    block_table: [seqs, max_pages].  Products and sums in float64 before each
+    rounding point."""
+    rows = q.shape[0]
+    G = NH // kvNH
+    scale = np.float32(1.0 / np.sqrt(np.float32(HS)))
+    out = np.zeros((rows, NH * HS), np.float32)
+    for r in range(rows):
+        L = int(pos[r]) + 1
+        pages = block_table[seq[r], :(L + 63) // 64]
+        K = kpool[pages].transpose(1, 0, 2, 3).reshape(kvNH, -1, HS)[:, :L].astype(np.float64)
+        V = vpool[pages].transpose(1, 0, 2, 3).reshape(kvNH, -1, HS)[:, :L].astype(np.float64)
+        for h in range(kvNH):
+            qg = q[r, h * G * HS:(h + 1) * G * HS].reshape(G, HS).astype(np.float64)
+            s = round_act((qg @ K[h].T).astype(np.float32), act)
+            x = s * scale
+            e = np.exp((x - x.max(axis=1, keepdims=True)).astype(np.float64)).astype(np.float32)
+            tot = e.astype(np.float64).sum(axis=1, keepdims=True).astype(np.float32)
+            P = round_act(round_act(e, act) * (np.float32(1.0) / tot), act)
+            out[r, h * G * HS:(h + 1) * G * HS] = round_act((P.astype(np.float64) @ V[h]).astype(np.float32),
+                                                           act).ravel()
+    return out
+
+
 def get_row(x, batch, row, col, idx):
     out = np.empty((batch, col), np.float32)
     lib().orc_get_row(_p(out), _p(_f32(x)), batch, row, col, idx)

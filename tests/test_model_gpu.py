@@ -78,16 +78,22 @@ def test_engine_prefill_decode_vs_oracle(dev, wtype, B, mk, monkeypatch):
     dm.free()
 
 
-@pytest.mark.parametrize("B,mk,fused", [(1, "0", "1"), (3, "0", "1"), (1, "0", "0"), (3, "0", "0"), (1, "1", "1"),
-                                        (3, "1", "1")])
-def test_engine_long_context_split_attention_vs_oracle(dev, B, mk, fused, monkeypatch):
-    """Decode at a 520..526-token context (9+ pages), where attention splits the
-    pages of each (sequence, kv head) over several CTAs (one launch whose
-    splits wait for each other, or two launches with WUKONG_SPLIT_ATTN_FUSED=0);
-    teacher-forced against the oracle like the short-context test.  mk=1: the
-    persistent kernel, whose attention splits each pair over co-resident CTAs."""
+@pytest.mark.parametrize("B,mk,attn", [(1, "0", "cluster"), (3, "0", "cluster"), (1, "0", "fused"), (3, "0", "fused"),
+                                       (1, "0", "two"), (3, "0", "two"), (1, "1", "cluster"), (3, "1", "cluster")])
+def test_engine_long_context_split_attention_vs_oracle(dev, B, mk, attn, monkeypatch):
+    """Decode at a 520..526-token context (9+ pages), where attention divides
+    the pages of each (sequence, kv head) over several CTAs: one thread-block
+    cluster per pair (default), or with WUKONG_CLUSTER_ATTN=0 split-K CTAs in
+    one launch whose splits wait for each other, or in two launches
+    (WUKONG_SPLIT_ATTN_FUSED=0); teacher-forced against the oracle like the
+    short-context test.  mk=1: the persistent kernel, whose attention splits
+    each pair over co-resident CTAs."""
     monkeypatch.setenv("WUKONG_MEGAKERNEL", mk)
-    monkeypatch.setenv("WUKONG_SPLIT_ATTN_FUSED", fused)
+    monkeypatch.setenv("WUKONG_SPLIT_ATTN_FUSED", "0" if attn == "two" else "1")
+    if attn == "cluster":
+        monkeypatch.delenv("WUKONG_CLUSTER_ATTN", raising=False)
+    else:
+        monkeypatch.setenv("WUKONG_CLUSTER_ATTN", "0")
     monkeypatch.delenv("WUKONG_SPLIT_ATTN", raising=False)
     cfg, ctx, n, steps = _cfg(1), 640, 520, 6
     w = make_weights(cfg, wk.Q8_0, wk.Q8_0, wk.F16, seed=11, ctx=ctx)
@@ -113,7 +119,7 @@ def test_engine_long_context_split_attention_vs_oracle(dev, B, mk, fused, monkey
                 ties += 1
     assert ties <= 1 + (B * steps) // 10
     # 1 layer: embed, qkv, attention (one launch, or scores + pv), o, fc, down, logits, advance
-    assert L.wk_model_step_launches(m) == (1 if mk == "1" else 1 + (5 if fused == "1" else 6) + ((B + 7) // 8) + 1)
+    assert L.wk_model_step_launches(m) == (1 if mk == "1" else 1 + (6 if attn == "two" else 5) + ((B + 7) // 8) + 1)
     L.wk_model_destroy(m)
     free(pids, ptok)
     dm.free()

@@ -72,6 +72,7 @@ EXT = {
     "wk_model_rows": (_I, [_P, _P]),
     "wk_model_set_sampling": (_I, [_P, _F, _I, _F, _U64]),
     "wk_sample_logits": (_I, [_P, _P, _I, _I, _I, _F, _I, _F, _U64, ctypes.c_longlong]),
+    "wk_attention_decode": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I]),
     "wk_fill_random_q8_0": (_I, [_P, _L, _I, _U64, _F]),
     "wk_fill_random_q4_0": (_I, [_P, _L, _I, _U64, _F]),
     "wk_fill_random_f16": (_I, [_P, _L, _U64, _F]),

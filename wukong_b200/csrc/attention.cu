@@ -454,6 +454,315 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(T *__restrict__ out
     }
 }
 
+// ---------------------------------------------------------------- decode attention over a CTA cluster
+// One thread-block cluster of CS CTAs per (row, KV head); CTA z of the
+// cluster takes the sequence's pages [z pps, (z + 1) pps).  The reference's
+// rounding points need the row maximum before any exponential, so the CTAs
+// exchange per-head values through distributed shared memory, separated by
+// hardware cluster barriers:
+//   1. s_j = T(q . k_j) for the own keys; the own maxima m_z (of s_j * scale)
+//      go to every CTA of the cluster; M = max_z m_z;
+//   2. e_j = exp(s_j * scale - M) stored as T in place; the own sums l_z of the
+//      unrounded e_j go to every CTA; sum = l_0 + l_1 + ... in z order;
+//   3. P_j = T(T(e_j) * (1 / sum)); the own partial o_z = P . V (fp32) goes to
+//      the owner CTA of each output element (element e of the [G][D] group
+//      output to CTA e % CS), which adds the CS partials in z order and stores
+//      T(o).
+// A cluster is scheduled as a unit and its CTAs wait only at the cluster
+// barriers, so clusters may run in any number of waves.  Old pages (before the
+// newest token's page) are requested before griddepcontrol.wait.
+constexpr int kClusterMax = 16;  // CTAs per cluster (above 8 is a non-portable size)
+
+struct ClusterSmem {
+    size_t ring, bars, qs, sc, pgs, red, xm, xl, xo, total;
+};
+__host__ __device__ inline ClusterSmem cluster_smem(int D, int S, int pps, int CS) {
+    ClusterSmem o;
+    size_t p = 0;
+    o.ring = p;
+    p += (size_t)S * kAttnPage * D * 2;
+    o.bars = p;
+    p += 16 * 8;
+    o.qs = p;
+    p += (size_t)8 * D * 2;
+    o.sc = p;
+    p += (size_t)8 * pps * kAttnPage * 2;
+    o.pgs = p;
+    p += ((size_t)pps * 4 + 15) / 16 * 16;
+    o.red = p;
+    p += 8 * 4 * 4;
+    o.xm = p;
+    p += (size_t)CS * 8 * 4;
+    o.xl = p;
+    p += (size_t)CS * 8 * 4;
+    o.xo = p;
+    p += (size_t)CS * ((8 * D + CS - 1) / CS) * 4;
+    o.total = p;
+    return o;
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// store v at the same shared-memory offset as `local` in CTA `rank` of the cluster
+__device__ __forceinline__ void st_cluster_f32(const float *local, uint32_t rank, float v) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(r), "f"(v) : "memory");
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) attn_cluster_kernel(T *__restrict__ out, long out_rs, const T *__restrict__ q,
+                                                           long q_rs, const int *__restrict__ seq_of_row,
+                                                           const int *__restrict__ pos_of_row, KVPaged kv, int G,
+                                                           int CS, int pps, int S, float scale, int *err, int early) {
+    Timeline tl;
+    constexpr int kPageBytes = kAttnPage * D * 2;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const ClusterSmem lay = cluster_smem(D, S, pps, CS);
+    uint8_t *ring = smem + lay.ring;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + lay.bars);
+    T *qs = reinterpret_cast<T *>(smem + lay.qs);
+    T *sc = reinterpret_cast<T *>(smem + lay.sc);
+    int *pgs = reinterpret_cast<int *>(smem + lay.pgs);
+    float *red = reinterpret_cast<float *>(smem + lay.red);  // [8 heads][4 warps]
+    float *xm = reinterpret_cast<float *>(smem + lay.xm);    // [CS][8] maxima of each CTA
+    float *xl = reinterpret_cast<float *>(smem + lay.xl);    // [CS][8] exponent sums of each CTA
+    float *xo = reinterpret_cast<float *>(smem + lay.xo);    // [CS][per] partial outputs of owned elements
+    const int per = (8 * D + CS - 1) / CS;
+    const int lpad = pps * kAttnPage;  // score row stride
+    const int z = (int)cluster_ctarank();
+    const int kvh = blockIdx.x / CS, row = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    // every CTA of the cluster has started before the first remote store (waited on below)
+    cluster_arrive_relaxed();
+    const int seq = seq_of_row[row], pos = pos_of_row[row];
+    const int L = pos + 1;
+    const int npages = (L + kAttnPage - 1) / kAttnPage;
+    const int pbeg = z * pps;
+    const int nloc = max(0, min(npages - pbeg, pps));  // own pages
+    const int total = 2 * nloc;                        // units: own K pages, then own V pages
+    const int newest = npages - 1 - pbeg;              // own index of the newest token's page (if in [0, nloc))
+    const T *K = reinterpret_cast<const T *>(kv.k);
+    const T *V = reinterpret_cast<const T *>(kv.v);
+    const int *bt = kv.block_table + (long)seq * kv.max_pages + pbeg;
+    auto page_src = [&](int u) -> const T * {
+        const int p = u < nloc ? u : u - nloc;
+        return (u < nloc ? K : V) + ((long)pgs[p] * kv.kv_heads + kvh) * (long)kAttnPage * D;
+    };
+    auto issue = [&](int u) {
+        const int sl = u % S;
+        mbar_expect_tx(bars + sl, kPageBytes);
+        bulk_g2s(ring + sl * kPageBytes, page_src(u), kPageBytes, bars + sl);
+    };
+    auto is_newest = [&](int u) { return (u < nloc ? u : u - nloc) == newest; };
+    if (tid < S) mbar_init(bars + tid, 1);
+    if (early)
+        for (int i = tid; i < nloc; i += 128) pgs[i] = bt[i];
+    mbar_fence_init();
+    __syncthreads();
+    const int first = min(S, total);
+    if (tid == 0 && early) {
+        // decode: pages other than the newest token's were written by earlier launches
+        for (int u = 0; u < first; ++u)
+            if (!is_newest(u)) issue(u);
+        for (int u = first; u < total; ++u)
+            if (!is_newest(u))
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(page_src(u)),
+                             "r"((uint32_t)kPageBytes)
+                             : "memory");
+    }
+    pdl_wait();
+    pdl_trigger();
+    tl.mark(104, npages, G);
+    if (!early) {
+        for (int i = tid; i < nloc; i += 128) pgs[i] = bt[i];
+        __syncthreads();
+    }
+    if (tid == 0)
+        for (int u = 0; u < first; ++u)
+            if (!early || is_newest(u)) issue(u);
+    stage_q<T, D>(qs, q + (long)row * q_rs + (long)kvh * G * D, G);
+    __syncthreads();
+    tl.phase(0);  // q staged
+    uint32_t qb[D / 16][2];
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+        qb[kk][0] = *reinterpret_cast<const uint32_t *>(qs + g * D + kk * 16 + 2 * t);
+        qb[kk][1] = *reinterpret_cast<const uint32_t *>(qs + g * D + kk * 16 + 2 * t + 8);
+    }
+
+    // ---- 1: own scores, rounded to T, and the own row max per head
+    float mx0 = -INFINITY, mx1 = -INFINITY;  // heads 2t, 2t+1
+    bool ok = true;
+    for (int p = 0; p < nloc; ++p) {
+        const int slot = p % S;
+        if (!mbar_wait_bounded(bars + slot, (p / S) & 1, err, 3)) ok = false;
+        const T *kt = reinterpret_cast<const T *>(ring + slot * kPageBytes) + warp * 16 * D;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ok) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(smem_u32(kt + (lane & 15) * D + kk * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
+                mma16<T>(c, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+            }
+        }
+        const int j0 = p * kAttnPage + warp * 16 + g;  // own key index
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = j0 + (i >> 1) * 8, h = 2 * t + (i & 1);
+            const bool valid = (pbeg * kAttnPage + j) < L;
+            const float sv = valid ? round_to<T>(c[i]) : -INFINITY;
+            sc[h * lpad + j] = from_float<T>(valid ? sv : 0.f);
+            if (i & 1)
+                mx1 = fmaxf(mx1, sv * scale);
+            else
+                mx0 = fmaxf(mx0, sv * scale);
+        }
+        __syncthreads();  // everyone is done with this slot
+        if (tid == 0 && p + S < total) issue(p + S);
+    }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+    }
+    if (g == 0) {
+        red[(2 * t) * 4 + warp] = mx0;
+        red[(2 * t + 1) * 4 + warp] = mx1;
+    }
+    __syncthreads();
+    cluster_wait();  // every CTA of the cluster runs
+    if (tid < CS * 8) {
+        const int h = tid & 7;
+        const float m = fmaxf(fmaxf(red[h * 4], red[h * 4 + 1]), fmaxf(red[h * 4 + 2], red[h * 4 + 3]));
+        st_cluster_f32(xm + z * 8 + h, tid >> 3, m);
+    }
+    cluster_arrive();
+    cluster_wait();
+    tl.phase(1);  // maxima exchanged
+    // ---- 2: numerators in place and the own exponent sums; thread -> (head h, keys i0, i0 + 16, ...)
+    const int h = tid >> 4, i0 = tid & 15;
+    float M = -INFINITY;
+    for (int zz = 0; zz < CS; ++zz) M = fmaxf(M, xm[zz * 8 + h]);
+    T *srow = sc + h * lpad;
+    const int nkeys = min(nloc * kAttnPage, max(0, L - pbeg * kAttnPage));  // own keys at or before pos
+    float lsum = 0.f;
+    for (int j0 = i0; j0 < nloc * kAttnPage; j0 += 16 * 8) {
+        float e[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = j0 + 16 * u;
+            e[u] = j < nkeys && h < G ? to_float(srow[j]) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = j0 + 16 * u;
+            if (j < nkeys && h < G) {
+                e[u] = expf(e[u] * scale - M);
+                lsum += e[u];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (j0 + 16 * u < nloc * kAttnPage) srow[j0 + 16 * u] = from_float<T>(e[u]);
+    }
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (i0 < CS) st_cluster_f32(xl + z * 8 + h, i0, lsum);
+    cluster_arrive();
+    cluster_wait();
+    tl.phase(2);  // sums exchanged
+    float sum = 0.f;
+    for (int zz = 0; zz < CS; ++zz) sum += xl[zz * 8 + h];
+    const float inv = 1.0f / sum;
+    if (h < G)
+        for (int j0 = i0; j0 < nkeys; j0 += 16 * 8) {
+            float e[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (j0 + 16 * u < nkeys) e[u] = to_float(srow[j0 + 16 * u]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (j0 + 16 * u < nkeys) srow[j0 + 16 * u] = from_float<T>(e[u] * inv);
+        }
+    __syncthreads();
+
+    // ---- 3: own partial O^T = V^T . P^T; warp w owns d-tiles w, w + 4
+    constexpr int kDT = D / 16;
+    constexpr int kA = kDT > 4 ? 2 : 1;
+    float o[kA][4];
+#pragma unroll
+    for (int a = 0; a < kA; ++a) o[a][0] = o[a][1] = o[a][2] = o[a][3] = 0.f;
+    for (int p = 0; p < nloc; ++p) {
+        const int u = nloc + p, slot = u % S;
+        if (!mbar_wait_bounded(bars + slot, (u / S) & 1, err, 3)) ok = false;
+        if (p == newest && L % kAttnPage) {
+            // rows past the sequence end hold stale cache bytes; their P is 0, but 0 * NaN is NaN
+            T *vw = reinterpret_cast<T *>(ring + slot * kPageBytes);
+            const int r0 = L - (pbeg + p) * kAttnPage;
+            for (int i = tid; i < (kAttnPage - r0) * D; i += 128) vw[r0 * D + i] = from_float<T>(0.f);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+        }
+        const T *vt = reinterpret_cast<const T *>(ring + slot * kPageBytes);
+        if (ok) {
+#pragma unroll
+            for (int ks = 0; ks < kAttnPage / 16; ++ks) {
+                const int key0 = p * kAttnPage + ks * 16;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(sc + g * lpad + key0 + 2 * t);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(sc + g * lpad + key0 + 2 * t + 8);
+#pragma unroll
+                for (int a = 0; a < kA; ++a) {
+                    const int d0 = (warp + 4 * a) * 16;
+                    if (d0 < D) {
+                        const int mi = lane >> 3, r = lane & 7;
+                        const T *addr = vt + (ks * 16 + r + (mi >> 1) * 8) * D + d0 + (mi & 1) * 8;
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4_t(smem_u32(addr), a0, a1, a2, a3);
+                        mma16<T>(o[a], a0, a1, a2, a3, b0, b1);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (tid == 0 && u + S < total) issue(u + S);
+    }
+    tl.phase(3);  // own P.V
+    // o[a]: rows d0 + g, d0 + g + 8; columns (heads) 2t, 2t + 1 -> owners
+#pragma unroll
+    for (int a = 0; a < kA; ++a) {
+        const int d0 = (warp + 4 * a) * 16;
+        if (d0 >= D) continue;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int d = d0 + g + (i >> 1) * 8, hh = 2 * t + (i & 1);
+            if (hh < G) {
+                const int e = hh * D + d;
+                st_cluster_f32(xo + z * per + e / CS, e % CS, o[a][i]);
+            }
+        }
+    }
+    cluster_arrive();
+    cluster_wait();
+    // owned elements e = z, z + CS, ...: partials added in z order
+    T *orow = out + (long)row * out_rs + (long)kvh * G * D;
+    for (int e = z + tid * CS; e < G * D; e += 128 * CS) {
+        float acc = 0.f;
+        for (int zz = 0; zz < CS; ++zz) acc += xo[zz * per + e / CS];
+        orow[e] = from_float<T>(acc);
+    }
+}
+
 // ---------------------------------------------------------------- split-K decode attention
 // For few (row, kv head) pairs and long contexts the pages are split over
 // gridDim.z CTAs in two launches with the reference's rounding points intact:
@@ -1175,6 +1484,65 @@ int launch_split(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_r
     return 2;
 }
 
+// Cluster decode attention (attn_cluster_kernel): CS CTAs per (row, KV head)
+// with CS about 2 x SMs / pairs (at most 16 and at most the context's pages),
+// pps pages per CTA, and a ring of S page slots (every own K and V page when
+// they fit).  Returns 0 when the shape or the device does not take it.
+template <typename T, int D>
+int launch_cluster(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
+                   int nrows, int max_len, const KVPaged &kv, int G, cudaStream_t s, bool pdl, bool early) {
+    const char *env = getenv("WUKONG_CLUSTER_ATTN");  // 0: the split / one-CTA kernels
+    if (env && env[0] == '0') return 0;
+    const int pages = (max_len + kAttnPage - 1) / kAttnPage;
+    const int pairs = nrows * kv.kv_heads;
+    if (pages < 1 || pairs < 1) return 0;
+    int CS = (2 * g_rt.num_sms + pairs - 1) / pairs;
+    if (CS < (pages + 47) / 48) CS = (pages + 47) / 48;  // at most 48 pages (their score rows) per CTA
+    if (CS > kClusterMax) CS = kClusterMax;
+    if (CS > pages) CS = pages;
+    int pps = (pages + CS - 1) / CS;
+    CS = (pages + pps - 1) / pps;
+    int S = 2 * pps < 16 ? 2 * pps : 16;
+    while (S > 2 && cluster_smem(D, S, pps, CS).total > (size_t)g_rt.max_smem_optin) --S;
+    const size_t smem = cluster_smem(D, S, pps, CS).total;
+    if (smem > (size_t)g_rt.max_smem_optin) return 0;
+    auto kern = attn_cluster_kernel<T, D>;
+    static int configured = 0;
+    if (!configured) {
+        WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        configured = 1;
+    }
+    static int smem_set = 0;
+    if ((int)smem > smem_set) {
+        WK_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        smem_set = (int)smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CS * kv.kv_heads, nrows);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (pdl && g_rt.pdl) ? 2 : 1;
+    // a cluster of CS CTAs must fit on one GPU processing cluster
+    int nclusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg) != cudaSuccess || nclusters < 1) {
+        cudaGetLastError();
+        return 0;
+    }
+    const float scale = 1.0f / sqrtf((float)D);
+    WK_CHECK(cudaLaunchKernelEx(&cfg, kern, out, out_rs, q, q_rs, seq_of_row, pos_of_row, kv, G, CS, pps, S, scale,
+                                g_rt.d_error, early ? 1 : 0));
+    return 1;
+}
+
 template <typename T, int D>
 void launch_decode_tc(T *out, long out_rs, const T *q, long q_rs, const int *seq_of_row, const int *pos_of_row,
                       int nrows, int max_len, const KVPaged &kv, int G, cudaStream_t s, bool pdl, const void *pf,
@@ -1480,6 +1848,15 @@ int attention_paged(T *out, long out_rs, const T *q, long q_rs, const int *seq_o
     if constexpr (sizeof(T) == 2) {
         if (c.page == kAttnPage && G <= 8 && (c.hd == 64 || c.hd == 128) && ((uintptr_t)c.k % 16) == 0 &&
             ((uintptr_t)c.v % 16) == 0) {
+            // decode rows: one cluster of CTAs per (row, KV head), unless one CTA each is asked for
+            const char *one = getenv("WUKONG_SPLIT_ATTN");
+            if (early && !(one && one[0] == '0')) {
+                const int nc = c.hd == 64 ? launch_cluster<T, 64>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows,
+                                                                   max_len, kv, G, s, pdl, early)
+                                          : launch_cluster<T, 128>(out, out_rs, q, q_rs, seq_of_row, pos_of_row,
+                                                                    nrows, max_len, kv, G, s, pdl, early);
+                if (nc) return nc;
+            }
             const int ns = !ws ? 0
                            : c.hd == 64 ? launch_split<T, 64>(out, out_rs, q, q_rs, seq_of_row, pos_of_row, nrows,
                                                               max_len, kv, G, s, pdl, early, *ws)

@@ -1091,6 +1091,34 @@ int wk_model_truncate(wk_model *m, int n) {
     return 0;
 }
 
+// The engine's decode attention over a paged K/V cache, callable on its own.
+int wk_attention_decode(void *out, const void *q, const void *kpool, const void *vpool, const int *block_table,
+                        int max_pages, const int *seq, const int *pos, int rows, int max_len, int n_heads,
+                        int kv_heads, int head_dim, int dtype) {
+    if (g_rt.device < 0) return fail("wk_attention_decode: cuda_init() has not been called");
+    if (!out || !q || !kpool || !vpool || !block_table || !seq || !pos || rows < 1 || max_len < 1 || kv_heads < 1 ||
+        n_heads % kv_heads || max_pages * kPage < max_len)
+        return fail("wk_attention_decode: bad arguments");
+    if (dtype != kF16 && dtype != kBF16) return fail("wk_attention_decode: dtype %d", dtype);
+    set_device_current();
+    PagedKV c;
+    c.k = const_cast<void *>(kpool);
+    c.v = const_cast<void *>(vpool);
+    c.block_table = block_table;
+    c.max_pages = max_pages;
+    c.page = kPage;
+    c.kv_heads = kv_heads;
+    c.hd = head_dim;
+    const long col = (long)n_heads * head_dim;
+    if (dtype == kF16)
+        attention_paged<__half>((__half *)out, col, (const __half *)q, col, seq, pos, rows, max_len, c, n_heads,
+                                stream(), true, nullptr, 0, true, nullptr);
+    else
+        attention_paged<__nv_bfloat16>((__nv_bfloat16 *)out, col, (const __nv_bfloat16 *)q, col, seq, pos, rows,
+                                       max_len, c, n_heads, stream(), true, nullptr, 0, true, nullptr);
+    return 0;
+}
+
 int wk_fill_random_q8_0(void *dst, long rows, int cols, uint64_t seed, float stdv) {
     if (cols % 32) return fail("cols must be a multiple of 32");
     ensure_init();

@@ -32,7 +32,8 @@ import numpy as np
 SLOTS, BLOCKS, STAMPS = 1024, 320, 9
 KINDS = {0: "store", 1: "resid", 2: "qkv", 3: "swiglu", 4: "logits", 5: "partial", 6: "all-reduce+resid",
          100: "attention",
-         101: "attention scores (split)", 102: "attention P.V (split)", 103: "attention (split, one launch)"}
+         101: "attention scores (split)", 102: "attention P.V (split)", 103: "attention (split, one launch)",
+         104: "attention (cluster)"}
 
 
 def record(model="1b", steps=12, prompt=None, batch=1):
