@@ -11,6 +11,8 @@ one call into the next.
 
 This file is named so that pytest collects it last.
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -89,3 +91,36 @@ def test_noalloc_predict_rejects_sizes_beyond_its_scratch(dev):
         assert dev.wk_predict_noalloc(p, p, p, p, B, Tn, d, V, EPS, wt) == -1
         assert words in dev.wk_last_error().decode()
     free(p)
+
+
+def _driver_memory():
+    """(free device bytes, bytes in use in the device's default stream-ordered
+    pool) through the CUDA driver, on the context the library made current."""
+    cu = ctypes.CDLL("libcuda.so.1")
+    free_b, total_b = ctypes.c_size_t(), ctypes.c_size_t()
+    assert cu.cuMemGetInfo_v2(ctypes.byref(free_b), ctypes.byref(total_b)) == 0
+    pool, used = ctypes.c_void_p(), ctypes.c_uint64()
+    assert cu.cuDeviceGetDefaultMemPool(ctypes.byref(pool), 0) == 0
+    CU_MEMPOOL_ATTR_USED_MEM_CURRENT = 7
+    assert cu.cuMemPoolGetAttribute(pool, CU_MEMPOOL_ATTR_USED_MEM_CURRENT, ctypes.byref(used)) == 0
+    return free_b.value, used.value
+
+
+def test_noalloc_predict_allocates_nothing(dev):
+    """After one call of each shape (which may load the kernels' code onto the
+    device), further calls of both shapes leave the device's free memory and
+    the default stream-ordered pool's usage unchanged."""
+    first = _case(Q8_0, B=3, Tn=2, d=2048, V=32000, seed=801)     # one pass
+    second = _case(F16, B=40, Tn=1, d=1024, V=8192, seed=901)     # five passes
+    o1, o2 = alloc(4 * first["B"]), alloc(4 * second["B"])
+    _noalloc(dev, first, o1)
+    _noalloc(dev, second, o2)
+    assert dev.wk_device_error(0) == 0  # synchronises the library stream
+    before = _driver_memory()
+    for _ in range(3):
+        _noalloc(dev, first, o1)
+        _noalloc(dev, second, o2)
+    got = down(o2, second["B"], np.int32)  # synchronises
+    assert _driver_memory() == before
+    assert (got >= 0).all() and (got < second["V"]).all()
+    free(o1, o2, *first["p"], *second["p"])
