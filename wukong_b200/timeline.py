@@ -18,7 +18,8 @@ its time goes (means over CTAs and launches, in microseconds):
           end = the CTA's last stamp.  N / K columns: the GEMV's shape;
           attention pages and query heads per KV head (split: pages, splits)
 
-Usage: python -m wukong_b200.timeline [--model 1b|8b] [--steps N] [--prompt P]
+Usage: python -m wukong_b200.timeline [--model 1b|8b|70b] [--steps N] [--prompt P] [--batch B]
+           [--shard N]  (rank 0's slice of an N-way split on this GPU alone, no exchanges)
        python -m torch.distributed.run --nproc-per-node N -m wukong_b200.timeline --model 8b
            (tensor-parallel over N GPUs; all-reduce+resid p5: first tile published)
 """
@@ -36,10 +37,12 @@ KINDS = {0: "store", 1: "resid", 2: "qkv", 3: "swiglu", 4: "logits", 5: "partial
          104: "attention (cluster)"}
 
 
-def record(model="1b", steps=12, prompt=None, batch=1):
+def record(model="1b", steps=12, prompt=None, batch=1, shard=1):
     """Under torch.distributed.run with more than one rank the model is
     tensor-parallel over the ranks (one per GPU); every rank records its own
-    launches."""
+    launches.  shard > 1 (one process): rank 0's slice of a model split over
+    `shard` ranks, run on this GPU alone without the exchanges (the per-rank
+    compute of tensor-parallel decode)."""
     import wukong_b200 as wk
     wk.LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libwukong_timeline.so")
     from wukong_b200.engine import LLAMA, Engine, SyntheticLlama
@@ -57,8 +60,8 @@ def record(model="1b", steps=12, prompt=None, batch=1):
         torch.distributed.broadcast(t, 0)
         wk.check(L.wk_tp_init(rank, world, bytes(t.numpy())))
     cfg = dict(LLAMA[model])
-    P = prompt or (128 if model == "1b" else 2048)
-    sm = SyntheticLlama(cfg, P + steps + 16, seed=1234, tp_rank=rank, tp_world=world)
+    P = prompt or {"1b": 128, "8b": 2048, "70b": 4096}[model]
+    sm = SyntheticLlama(cfg, P + steps + 16, seed=1234, tp_rank=rank, tp_world=world if world > 1 else shard)
     eng = Engine.from_synthetic(sm, max_batch=batch, tp=world > 1)
     ids = np.random.default_rng(7).integers(0, cfg["V"], size=(batch, P)).astype(np.int32)
     d = L.cuda_malloc(ids.nbytes)
@@ -121,15 +124,19 @@ def _mean(vs):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--model", default="1b", choices=["1b", "8b"])
+    ap.add_argument("--model", default="1b", choices=["1b", "8b", "70b"])
     ap.add_argument("--steps", type=int, default=12)
     ap.add_argument("--prompt", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--shard", type=int, default=1,
+                    help="one process: rank 0's slice of the model split over this many ranks, no exchanges")
     a = ap.parse_args(argv)
-    info, stamps, n, res, lps = record(a.model, a.steps, a.prompt)
+    info, stamps, n, res, lps = record(a.model, a.steps, a.prompt, a.batch, a.shard)
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
     rows, span_us, nev = summarize(info, stamps, n)
-    print(f"model {a.model}: {nev} GEMV / attention launches recorded over {span_us:.1f} us ({a.steps} decode "
+    print(f"model {a.model}" + (f" (rank 0 of {a.shard}, no exchanges)" if a.shard > 1 else "") +
+          f", batch {a.batch}: {nev} GEMV / attention launches recorded over {span_us:.1f} us ({a.steps} decode "
           f"steps of {lps} launches; %globaltimer step {res} ns)")
     print("| launch | N | K | CTAs | count | gap | active | tail | head | p0 | p1 | p2 | p3 | p4 | p5 | end |")
     print("|---|---|---|---|---|---|---|---|---|---|---|---|---|---|---|---|")
