@@ -1496,13 +1496,29 @@ int launch_cluster(T *out, long out_rs, const T *q, long q_rs, const int *seq_of
     const int pages = (max_len + kAttnPage - 1) / kAttnPage;
     const int pairs = nrows * kv.kv_heads;
     if (pages < 1 || pairs < 1) return 0;
+    // The largest cluster: 16 CTAs for at most 4 pairs (tensor-parallel ranks hold 1-4 KV heads at batch
+    // 1; one cluster then spreads a long context over many SMs), 8 otherwise -- a 16-CTA cluster of
+    // large CTAs needs 16 free SMs of one processing cluster at once, and 8 such clusters started in
+    // staggered waves (Llama-3.1-70B, batch 8, one KV head per rank: attention 34.5 -> 24.5 us per
+    // layer with 8).  WUKONG_CLUSTER_MAX and WUKONG_CLUSTER_SLOTS (the deepest page ring) override.
+    static const int cs_env = [] {
+        const char *e = getenv("WUKONG_CLUSTER_MAX");
+        const int v = e ? atoi(e) : 0;
+        return v >= 1 && v <= kClusterMax ? v : 0;
+    }();
+    const int cs_max = cs_env ? cs_env : (pairs <= 4 ? kClusterMax : 8);
+    static const int s_max = [] {
+        const char *e = getenv("WUKONG_CLUSTER_SLOTS");
+        const int v = e ? atoi(e) : 0;
+        return v >= 2 && v <= 16 ? v : 16;
+    }();
     int CS = (2 * g_rt.num_sms + pairs - 1) / pairs;
     if (CS < (pages + 47) / 48) CS = (pages + 47) / 48;  // at most 48 pages (their score rows) per CTA
-    if (CS > kClusterMax) CS = kClusterMax;
+    if (CS > cs_max) CS = cs_max;
     if (CS > pages) CS = pages;
     int pps = (pages + CS - 1) / CS;
     CS = (pages + pps - 1) / pps;
-    int S = 2 * pps < 16 ? 2 * pps : 16;
+    int S = 2 * pps < s_max ? 2 * pps : s_max;
     while (S > 2 && cluster_smem(D, S, pps, CS).total > (size_t)g_rt.max_smem_optin) --S;
     const size_t smem = cluster_smem(D, S, pps, CS).total;
     if (smem > (size_t)g_rt.max_smem_optin) return 0;

@@ -79,6 +79,7 @@ struct Runtime {
     bool pdl = true;      // programmatic dependent launch on the hot kernels
     bool tc_gemm = true;  // tcgen05 GEMM for activation blocks of >= 16 rows
     int warp_tile_min = 4096;  // SwiGLU / logits layers with this many 16-row tiles run one tile per warp
+    long l2_prefetch_max = 12L << 20;  // engine: bytes of the next layer's weights each linear layer prefetches into L2
     // limit of the cross-GPU flag waits of the tensor-parallel exchange
     // (WUKONG_WAIT_LIMIT_MS, default one second)
     unsigned long long wait_limit_ns = 1000000000ull;

@@ -289,7 +289,6 @@ int reduce_partials(wk_model *m, int rows, cudaStream_t s) {
 // Run the layers and the logits head on `rows` activation rows in m->x.
 // Row i belongs to sequence seq[i] at position pos[i]; max_len bounds the
 // attention length.  Returns the number of kernel launches.
-constexpr long kL2PrefetchMax = 12L << 20;
 
 // Prefill of sequences of different lengths (continuous batching): group i
 // holds activation rows [row0[i], row0[i] + len[i]) of the sequence in slot
@@ -319,11 +318,12 @@ int run_layers(wk_model *m, int rows, const int *seq, const int *pos, int max_le
     // prefetches the head of the logits matrix.  Attention prefetches nothing
     // (its few CTAs would queue the prefetches ahead of their own page loads).
     auto wbytes = [&](long rows, int K, int wt) -> long { return rows * quant_row_bytes(wt, K); };
-    // At most kL2PrefetchMax bytes ahead: a larger prefetch queues ahead of the
-    // next kernel's own activation loads in the memory system (measured, 8B:
-    // 58 MB ahead of up|gate delayed its prologue by ~5 us; 12 MB: 2.79 -> 2.67
-    // ms/step)
-    auto capped = [](long b) -> long { return b < kL2PrefetchMax ? b : kL2PrefetchMax; };
+    // At most g_rt.l2_prefetch_max bytes ahead (12 MB; WUKONG_L2_PREFETCH_MB):
+    // a larger prefetch queues ahead of the next kernel's own activation loads
+    // in the memory system (measured, 8B: 58 MB ahead of up|gate delayed its
+    // prologue by ~5 us; 12 MB: 2.79 -> 2.67 ms/step)
+    const long pf_max = g_rt.l2_prefetch_max;
+    auto capped = [pf_max](long b) -> long { return b < pf_max ? b : pf_max; };
     const int W = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
     // Below kTcMinRows every linear layer here runs on the GEMV, so the launch
     // before each GEMV is a GEMV, an attention kernel (both trigger their

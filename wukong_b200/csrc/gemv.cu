@@ -229,9 +229,10 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 // RMSNorm weights held in registers from before griddepcontrol.wait (they do
-// not depend on the previous kernel): thread t takes k = 4 (t + 256 j), j < 4,
-// which covers K <= 4096; larger K loads the rest after the wait.
-constexpr int kNormRegs = 4;
+// not depend on the previous kernel): thread t takes k = 4 (t + 256 j), j < 8,
+// which covers K <= 8192 (Llama-3.1-70B); larger K loads the rest after the
+// wait.
+constexpr int kNormRegs = 8;
 struct NormW {
     float4 v[kNormRegs];
 };
@@ -252,7 +253,7 @@ __device__ __forceinline__ void norm_pre(const GemvArgs &a, NormW &nw) {
 // Sum-of-squares order (the persistent kernel follows it too): thread t adds
 // the quads (4 consecutive values) k/4 = t, t + 256, ... of a row in that order,
 // its warp sums the threads by butterfly, then the 8 warps' sums are added in
-// warp order.  One row (decode) with K <= 4096 stays in registers from the load
+// warp order.  One row (decode) with K <= 8192 stays in registers from the load
 // to the normalised store; more rows go through shared memory in the same order.
 template <typename T>
 __device__ __forceinline__ void quad_ss(uint2 q, float &ss) {
@@ -308,15 +309,19 @@ __device__ void stage_xn(const GemvArgs &a, const Smem &sm, int Kpad, const Norm
         }
         return;  // the caller's barrier publishes the rows
     }
-    for (int i = tid; i < total; i += 8 * nt) {  // up to 8 loads in flight per thread
-        uint2 v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (i + j * nt < total) v[j] = ld(i + j * nt);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (i + j * nt < total) sm.xn[i + j * nt] = v[j];
+    // every quad of every row in flight at once (8-byte asynchronous copies, then
+    // one wait): several rows of a wide layer cost one L2 round trip, not one per
+    // batch of loads a thread can hold in registers
+    for (int i = tid; i < total; i += nt) {
+        const int m = i / nq, k = (i - m * nq) * 4;
+        if (k < a.K)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(&sm.xn[i])),
+                         "l"(x + (long)m * a.ldx + k)
+                         : "memory");
+        else
+            sm.xn[i] = make_uint2(0u, 0u);
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     if (!a.norm_w) return;
     for (int m = 0; m < M; ++m) {
@@ -497,11 +502,15 @@ __device__ void exchange_tile(const GemvArgs &a, const Smem &sm, int tile, const
     }
     __syncthreads();
     const unsigned long long e = *e_s;
-    // word (parity, tile, source rank, tid) of a receiver's buffer
+    // word (parity, tile, source rank, tid) of a receiver's buffer; only the
+    // words of real outputs (activation rows m < M, rows inside N) are pushed
+    // and awaited -- at batch 1, 16 of the tile's 128
     const size_t base = ((size_t)(e & 1) * kTpMaxTiles + tile) * kTpMaxWorld * 128 + tid;
+    const int r = (tid >> 3) & 15, m = tid & 7;
+    const bool valid = tid < 128 && m < a.M && row_valid(a, tile, r);
     float own = 0.f;
-    if (tid < 128) {
-        own = tile_sum(sm.red, tid >> 3, tid & 7);
+    if (valid) {
+        own = tile_sum(sm.red, r, m);
         const unsigned long long w = ll_word(__float_as_uint(own), e);
         for (int q = 0; q < L.world; ++q)
             if (q != L.rank)
@@ -509,9 +518,7 @@ __device__ void exchange_tile(const GemvArgs &a, const Smem &sm, int tile, const
     }
     tl.phase(5);  // first tile pushed
     __syncthreads();  // e_s is rewritten by the next tile
-    if (tid >= 128) return;
-    const int r = tid >> 3, m = tid & 7;
-    const bool valid = m < a.M && row_valid(a, tile, r);
+    if (!valid) return;
     const unsigned long long *mine = reinterpret_cast<const unsigned long long *>(L.peers[L.rank] + kXTileLL) + base;
     float acc = 0.f;
     bool ok = true;
@@ -531,7 +538,6 @@ __device__ void exchange_tile(const GemvArgs &a, const Smem &sm, int tile, const
         atomicCAS(a.err, 0, 42);
         return;
     }
-    if (!valid) return;
     const int n = tile_row(a, tile, r);
     const float res = pre ? pre->s0 : to_float(reinterpret_cast<const T *>(a.res)[(long)m * a.ldr + n]);
     reinterpret_cast<T *>(a.out)[(long)m * a.ldo + n] = from_float<T>(res + round_to<T>(acc));

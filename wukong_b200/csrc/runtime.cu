@@ -93,6 +93,8 @@ void cuda_init(int idx) {
     g_rt.tc_gemm = !(tc && tc[0] == '0');
     const char *wt = getenv("WUKONG_WARP_TILE_MIN");
     if (wt && atoi(wt) > 0) g_rt.warp_tile_min = atoi(wt);
+    const char *pfm = getenv("WUKONG_L2_PREFETCH_MB");
+    if (pfm && atoi(pfm) >= 0) g_rt.l2_prefetch_max = (long)atoi(pfm) << 20;
     const char *wl = getenv("WUKONG_WAIT_LIMIT_MS");
     if (wl && atoi(wl) > 0) g_rt.wait_limit_ns = 1000000ull * (unsigned long long)atoi(wl);
     // split-K partials of the tcgen05 GEMM: at most 2 CTAs per SM of 128 x 64 fp32 tiles

@@ -63,7 +63,9 @@ def record(model="1b", steps=12, prompt=None, batch=1, shard=1):
     P = prompt or {"1b": 128, "8b": 2048, "70b": 4096}[model]
     sm = SyntheticLlama(cfg, P + steps + 16, seed=1234, tp_rank=rank, tp_world=world if world > 1 else shard)
     eng = Engine.from_synthetic(sm, max_batch=batch, tp=world > 1)
-    ids = np.random.default_rng(7).integers(0, cfg["V"], size=(batch, P)).astype(np.int32)
+    # token ids within the engine's vocabulary (a one-process shard has the rank's slice of it)
+    vocab = cfg["V"] if world > 1 else sm.local["V"]
+    ids = np.random.default_rng(7).integers(0, vocab, size=(batch, P)).astype(np.int32)
     d = L.cuda_malloc(ids.nbytes)
     L.cuda_to_device(d, ids.ctypes.data_as(ctypes.c_void_p), ids.nbytes)
     eng.prefill(d, batch, P)
