@@ -229,10 +229,13 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 // RMSNorm weights held in registers from before griddepcontrol.wait (they do
-// not depend on the previous kernel): thread t takes k = 4 (t + 256 j), j < 8,
-// which covers K <= 8192 (Llama-3.1-70B); larger K loads the rest after the
-// wait.
-constexpr int kNormRegs = 8;
+// not depend on the previous kernel): thread t takes k = 4 (t + 256 j), j < 4,
+// which covers K <= 4096; larger K loads the rest in the normalise loop (one
+// L2 round trip per row and quad: at Llama-3.1-70B's K = 8192 and 4 rows about
+// 11 us of prologue per normalising launch).  Eight register quads, or four
+// more loaded beside the row copies, cover K = 8192 but cost the 1B decode
+// step 4.4 % and the 8B step 1.6 % (registers held across the wait).
+constexpr int kNormRegs = 4;
 struct NormW {
     float4 v[kNormRegs];
 };
@@ -253,7 +256,7 @@ __device__ __forceinline__ void norm_pre(const GemvArgs &a, NormW &nw) {
 // Sum-of-squares order (the persistent kernel follows it too): thread t adds
 // the quads (4 consecutive values) k/4 = t, t + 256, ... of a row in that order,
 // its warp sums the threads by butterfly, then the 8 warps' sums are added in
-// warp order.  One row (decode) with K <= 8192 stays in registers from the load
+// warp order.  One row (decode) with K <= 4096 stays in registers from the load
 // to the normalised store; more rows go through shared memory in the same order.
 template <typename T>
 __device__ __forceinline__ void quad_ss(uint2 q, float &ss) {
@@ -962,7 +965,13 @@ void gemv(GemvArgs a, int act, cudaStream_t s) {
     // preferred (16 warps per SM hide more latency than deeper rings)
     size_t smem_used = smem;
     int ns = kStages;
-    if (2 * (smem + 1024) > (size_t)g_rt.smem_per_sm) {
+    // 2-stage rings only where they buy a second CTA per SM: a launch of at most one tile per SM
+    // whose warps stream more units than 2 slots hold (e.g. a 2048-row down projection over
+    // K = 8192: 128 tiles, 4 units per warp) keeps 3 (1B decode 0.690 -> 0.649 ms/step; 6 slots,
+    // 231 KB, measured 0.711)
+    const int units = (a.K / 256 + kWarps - 1) / kWarps;  // per warp and tile (CTA tiles)
+    const bool one_per_sm = ntiles <= g_rt.num_sms && units > 2;
+    if (!one_per_sm && 2 * (smem + 1024) > (size_t)g_rt.smem_per_sm) {
         const size_t smem2 = gemv_smem_bytes(a.K, a.M, a.wtype, a.norm_w != nullptr, 2);
         if (2 * (smem2 + 1024) <= (size_t)g_rt.smem_per_sm) {
             smem_used = smem2;
