@@ -1501,17 +1501,18 @@ int launch_cluster(T *out, long out_rs, const T *q, long q_rs, const int *seq_of
     // large CTAs needs 16 free SMs of one processing cluster at once, and 8 such clusters started in
     // staggered waves (Llama-3.1-70B, batch 8, one KV head per rank: attention 34.5 -> 24.5 us per
     // layer with 8).  WUKONG_CLUSTER_MAX and WUKONG_CLUSTER_SLOTS (the deepest page ring) override.
-    static const int cs_env = [] {
+    // (constant-initialised statics, read on first use: no guarded initialisation, so the static
+    // archive needs no C++ runtime)
+    static int cs_env = -1, s_max = -1;
+    if (cs_env < 0) {
         const char *e = getenv("WUKONG_CLUSTER_MAX");
         const int v = e ? atoi(e) : 0;
-        return v >= 1 && v <= kClusterMax ? v : 0;
-    }();
+        cs_env = v >= 1 && v <= kClusterMax ? v : 0;
+        const char *f = getenv("WUKONG_CLUSTER_SLOTS");
+        const int w = f ? atoi(f) : 0;
+        s_max = w >= 2 && w <= 16 ? w : 16;
+    }
     const int cs_max = cs_env ? cs_env : (pairs <= 4 ? kClusterMax : 8);
-    static const int s_max = [] {
-        const char *e = getenv("WUKONG_CLUSTER_SLOTS");
-        const int v = e ? atoi(e) : 0;
-        return v >= 2 && v <= 16 ? v : 16;
-    }();
     int CS = (2 * g_rt.num_sms + pairs - 1) / pairs;
     if (CS < (pages + 47) / 48) CS = (pages + 47) / 48;  // at most 48 pages (their score rows) per CTA
     if (CS > cs_max) CS = cs_max;
